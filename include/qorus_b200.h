@@ -1,0 +1,112 @@
+/*
+ * qorus_b200.h — additive entry points of libqorus_b200.so.
+ *
+ * The upstream API (qorus.h) is unchanged; nothing here is needed to use
+ * it.  These calls exist for callers that want to keep data on the device
+ * (device pointers in and out, an explicit CUDA stream), for the synthetic
+ * model/KV generators the parity tests and benchmarks share, and for
+ * tensor-parallel setup.  Streams are passed as `void*` (a cudaStream_t;
+ * NULL = the legacy default stream) so the header needs no CUDA include.
+ *
+ * Each declaration names the upstream interface it stands beside.
+ */
+#ifndef QORUS_B200_H
+#define QORUS_B200_H
+
+#include "qorus.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- synthetic inputs (host, deterministic, multi-threaded) ------------
+ * Counter-based: value i of stream s under seed k is a pure function of
+ * (k, s, i), so any slice can be generated independently and the CPU
+ * oracle and the device path see identical bytes.  Stand-in for the
+ * upstream dummy-model writer tools/convert_llama.py:116-239, which wrote
+ * FP32 noise where Q4_0 was expected; these write real Q4_0 blocks in the
+ * [out][in] orientation (file order upstream src/models/model.c:355-619). */
+
+/* Bytes of a .qorus v2 file for cfg (64-byte header + 64-byte padded tensors). */
+size_t q_b200_model_file_size(const q_llama_config* cfg);
+
+/* Write a random-init model: embeddings and output N(0,0.02), norm gains
+ * 1+N(0,0.02), linear layers Q4_0 with nibbles uniform 0..15 and scales
+ * uniform [0.001,0.01].  n_threads <= 0 means all online CPUs. */
+q_error_code q_b200_write_model_file(const char* path, const q_llama_config* cfg,
+                                     uint64_t seed, int n_threads);
+
+/* out[j] = mean + stddev * N(0,1)[first_index + j] of stream `stream`. */
+void q_b200_fill_normal(float* out, size_t n, uint64_t seed, uint64_t stream,
+                        uint64_t first_index, float mean, float stddev, int n_threads);
+
+/* out[j] = uniform integer in [0, modulus) drawn from (seed, stream, first_index+j). */
+void q_b200_fill_tokens(uint32_t* out, size_t n, uint64_t seed, uint64_t stream,
+                        uint64_t first_index, uint32_t modulus);
+
+/* Q4_0 blocks with nibbles uniform 0..15 and scale uniform [smin, smax). */
+void q_b200_fill_q4(q_block_q4_0* out, size_t n_blocks, uint64_t seed, uint64_t stream,
+                    uint64_t first_block, float smin, float smax, int n_threads);
+
+/* Fill positions [0, n_pos) of a HOST KV image in the upstream cache layout
+ * [n_layers][n_kv_heads][max_seq_len][K(head_dim) | V(head_dim)] fp32
+ * (upstream src/models/model.c:700-740) with N(0,1); other positions are
+ * left untouched. */
+q_error_code q_b200_fill_kv_prefill(float* kv_host, const q_llama_config* cfg,
+                                    uint32_t n_pos, uint64_t seed, int n_threads);
+
+/* ---- KV cache access (tier 2 lives in HBM) ----------------------------- */
+
+/* Copy bytes between a host buffer and the device KV cache at a byte
+ * offset into the upstream layout. */
+q_error_code q_b200_kv_write(q_context* ctx, size_t offset, const void* host, size_t bytes);
+q_error_code q_b200_kv_read(q_context* ctx, size_t offset, void* host, size_t bytes);
+
+/* ---- device-resident decode -------------------------------------------- */
+
+/* The CUDA stream every model kernel of this context runs on. */
+void* q_b200_stream(q_context* ctx);
+
+/* One greedy decode step like llama_forward(model, ctx, &token, 1, pos, …)
+ * followed by q_sample_token(temperature 0), but the argmax runs on the
+ * device and only the 4-byte token crosses PCIe. */
+q_error_code q_b200_decode_greedy(q_llama_model* model, q_context* ctx, uint32_t token,
+                                  uint32_t pos, uint32_t* next_token);
+
+/* n_steps greedy decode steps replayed from the captured per-token CUDA
+ * graph, the token fed back on the device; out_tokens[i] (host) receives
+ * step i's argmax.  Asynchronous unless `sync` is non-zero; out_tokens is
+ * written only when sync != 0. */
+q_error_code q_b200_decode_loop(q_llama_model* model, q_context* ctx, uint32_t first_token,
+                                uint32_t pos, uint32_t n_steps, uint32_t* out_tokens, int sync);
+
+/* Device logits of the last forward / decode step ([vocab] fp32). */
+const float* q_b200_device_logits(q_context* ctx);
+
+/* ---- kernel entry points on device buffers ------------------------------
+ * The Q4_0 GEMV of upstream src/ops/avx2/matmul.c:98-271 on device memory.
+ * Weights are first repacked from the upstream 20-byte AoS blocks into the
+ * device stream layout (tiles of rows; 16-byte nibble planes then fp32
+ * scales per tile). */
+size_t q_b200_q4_packed_bytes(uint32_t M, uint32_t K);
+q_error_code q_b200_q4_pack(const q_block_q4_0* d_src, uint32_t M, uint32_t K,
+                            void* d_dst, void* stream);
+q_error_code q_b200_gemv_q4(const void* d_packed, uint32_t M, uint32_t K,
+                            const float* d_x, float* d_y, void* stream);
+
+/* FP32 GEMV y[M] = W[M,K] x[K] (the LM head of upstream
+ * src/models/model.c:1821-1844, dot order of src/ops/avx2/matmul_fp32.c). */
+q_error_code q_b200_gemv_f32(const float* d_w, uint32_t M, uint32_t K,
+                             const float* d_x, float* d_y, void* stream);
+
+/* Number of kernels this library launched since load (all entry points). */
+uint64_t q_b200_kernel_launches(void);
+
+/* Last CUDA error string seen by the library ("" if none). */
+const char* q_b200_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QORUS_B200_H */
