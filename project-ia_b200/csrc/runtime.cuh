@@ -1,0 +1,111 @@
+// runtime.cuh — host-side state shared by the parts of libqorus_b200.so:
+// launch plans, per-context device state, error plumbing.
+#pragma once
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "attn_decode.cuh"
+#include "gemv_q4.cuh"
+#include "head.cuh"
+#include "ops.cuh"
+#include "qorus_b200.h"
+
+namespace qb200 {
+
+// ---- errors / counters ------------------------------------------------------
+
+void set_last_error(const char* where, cudaError_t e);
+bool cuda_ok(cudaError_t e, const char* where);
+const char* last_error_cstr();
+extern std::atomic<uint64_t> g_kernel_launches;
+int device_sms();
+cudaStream_t op_stream();  // stream for the kernel-level entry points
+
+#define Q_CUDA(call)                                                    \
+    do {                                                                \
+        if (!::qb200::cuda_ok((call), #call)) return Q_ERR_INVALID_ARG; \
+    } while (0)
+
+// ---- GEMV launch plan ---------------------------------------------------------
+
+struct GemvPlan {
+    uint32_t M = 0, K = 0, R = 0, c = 0, bpt = 0, n_tiles = 0, grid = 0, threads = 0;
+    size_t smem = 0, packed_bytes = 0;
+};
+
+bool plan_gemv(uint32_t M, uint32_t K, bool pairs, GemvPlan& p);
+cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, cudaStream_t s, bool pdl);
+cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,
+                    uint8_t* d_dst, cudaStream_t s);
+
+template <typename Kern, typename Args>
+cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                      const Args& args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+// ---- per-context device state ----------------------------------------------------
+
+struct DevState {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    // tier 3 device twin
+    uint8_t* arena = nullptr;
+    size_t arena_size = 0, arena_head = 0, arena_base = 0;
+    // model (tier 1 in HBM)
+    bool built = false;
+    q_llama_config cfg{};
+    uint32_t hd = 0, kvd = 0, n_chunks = 0;
+    std::vector<uint8_t*> qkv, wo, gu, down;
+    GemvPlan p_qkv, p_wo, p_gu, p_down;
+    float* attn_norm = nullptr;  // [L][D]
+    float* ffn_norm = nullptr;   // [L][D]
+    float* out_norm = nullptr;
+    float* embd = nullptr;
+    float* out_w = nullptr;
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    std::vector<void*> weight_allocs;
+    // activations (device arena, below the watermark)
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
+    float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr;
+    float* logits = nullptr;
+    uint32_t* ticket = nullptr;
+    unsigned long long* best = nullptr;
+    StepParams* step = nullptr;
+    uint32_t *tok_out = nullptr, *tok_count = nullptr, *last_tok = nullptr;
+    uint32_t tok_cap = 0;
+    StepParams* h_step = nullptr;  // pinned, one per row of a call
+    // captured graphs (valid for graph_kv)
+    void* graph_kv = nullptr;
+    cudaGraphExec_t g_body = nullptr, g_full = nullptr;
+    uint64_t kernels_body = 0, kernels_full = 0;
+};
+
+DevState* state_of(const q_context* ctx, bool create);
+void state_erase(const q_context* ctx);
+void* dev_arena_alloc(DevState* s, size_t bytes);
+
+q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* model);
+q_error_code ensure_graphs(q_context* ctx, DevState* s);
+q_error_code check_device_status(const char* where);
+void free_model(DevState* s);
+
+}  // namespace qb200
