@@ -1,0 +1,324 @@
+// api_model.cu — llama_build_graph / llama_forward / q_generate on the B200,
+// and the device-resident decode entry points of qorus_b200.h.
+#include <cmath>
+#include <cstdlib>
+
+#include "runtime.cuh"
+
+using namespace qb200;
+
+static size_t al64(size_t n) { return (n + 63) & ~(size_t)63; }
+
+// Host tensor view in the host arena, bounds-checked against the mmap
+// (upstream create_tensor_view, model.c:170-292).  Views use the [out][in]
+// orientation the device kernels read (ne[0] = rows, ne[1] = columns).
+static q_tensor* make_view(q_context* ctx, size_t off, uint32_t ne0, uint32_t ne1, q_dtype t,
+                           const char* name) {
+    size_t bytes = t == Q_F32 ? (size_t)ne0 * ne1 * 4 : (size_t)ne0 * (ne1 / 32) * 20;
+    if (bytes == 0 || off + bytes > ctx->weights_size) return nullptr;
+    q_tensor* v = (q_tensor*)q_arena_alloc(ctx, sizeof(q_tensor));
+    if (!v) return nullptr;
+    memset(v, 0, sizeof *v);
+    v->data = (uint8_t*)ctx->weights_mmap + off;
+    v->ne[0] = ne0;
+    v->ne[1] = ne1;
+    v->ne[2] = v->ne[3] = 1;
+    v->type = t;
+    if (t == Q_F32) {
+        v->nb[3] = v->nb[2] = 4;
+        v->nb[1] = 4;
+        v->nb[0] = (size_t)ne1 * 4;
+    } else {
+        v->nb[0] = (size_t)(ne1 / 32) * 20;
+        v->nb[1] = v->nb[2] = v->nb[3] = 20;
+    }
+    strncpy(v->name, name, sizeof v->name - 1);
+    return v;
+}
+
+extern "C" {
+
+q_error_code llama_build_graph(q_context* ctx, q_llama_model* model) {
+    // validation order of upstream model.c:294-343
+    if (!ctx || !model) return Q_ERR_NULL_PTR;
+    if (!ctx->weights_mmap || !ctx->header) return Q_ERR_NULL_PTR;
+    const q_model_header* h = ctx->header;
+    if (h->magic != Q_MAGIC) return Q_ERR_INVALID_MAGIC;
+    if (!h->n_layers || !h->dim || !h->vocab_size || !h->n_heads || !h->n_kv_heads)
+        return Q_ERR_INVALID_CONFIG;
+    if (h->dim % 32 || h->hidden_dim % 32) return Q_ERR_INVALID_CONFIG;
+    if (h->dim % h->n_heads || h->n_heads % h->n_kv_heads || !h->hidden_dim || !h->max_seq_len)
+        return Q_ERR_INVALID_CONFIG;
+    q_llama_config& c = model->config;
+    c.vocab_size = h->vocab_size;
+    c.dim = h->dim;
+    c.hidden_dim = h->hidden_dim;
+    c.n_layers = h->n_layers;
+    c.n_heads = h->n_heads;
+    c.n_kv_heads = h->n_kv_heads;
+    c.max_seq_len = h->max_seq_len;
+    c.rope_freq_base = h->rope_freq_base;
+    c.rms_norm_eps = (h->version >= 2 && h->rms_norm_eps > 0.0f) ? h->rms_norm_eps : 1e-5f;
+    model->ctx = ctx;
+    const uint32_t D = c.dim, H = c.hidden_dim, V = c.vocab_size;
+    const uint32_t hd = D / c.n_heads, kvd = c.n_kv_heads * hd;
+    size_t off = Q_HEADER_SIZE;
+#define VIEW(dst, n0, n1, t, nm)                                             \
+    do {                                                                     \
+        size_t by = (t) == Q_F32 ? (size_t)(n0) * (n1) * 4                   \
+                                 : (size_t)(n0) * ((n1) / 32) * 20;          \
+        if (off + al64(by) > ctx->weights_size) return Q_ERR_INVALID_CONFIG; \
+        dst = make_view(ctx, off, n0, n1, t, nm);                            \
+        if (!dst) return Q_ERR_ARENA_OOM;                                    \
+        off += al64(by);                                                     \
+    } while (0)
+    VIEW(model->token_embd, V, D, Q_F32, "token_embd.weight");
+    VIEW(model->output_norm, D, 1, Q_F32, "output_norm.weight");
+    VIEW(model->output, V, D, Q_F32, "output.weight");
+    model->layers = (q_llama_layer*)q_arena_alloc(ctx, sizeof(q_llama_layer) * c.n_layers);
+    if (!model->layers) return Q_ERR_ARENA_OOM;
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+        q_llama_layer* ly = &model->layers[l];
+        memset(ly, 0, sizeof *ly);
+        ly->layer_idx = l;
+        VIEW(ly->attn_norm, D, 1, Q_F32, "attn_norm.weight");
+        VIEW(ly->wq, D, D, Q_Q4_0, "wq.weight");
+        VIEW(ly->wk, kvd, D, Q_Q4_0, "wk.weight");
+        VIEW(ly->wv, kvd, D, Q_Q4_0, "wv.weight");
+        VIEW(ly->wo, D, D, Q_Q4_0, "wo.weight");
+        VIEW(ly->ffn_norm, D, 1, Q_F32, "ffn_norm.weight");
+        VIEW(ly->w_gate, H, D, Q_Q4_0, "w_gate.weight");
+        VIEW(ly->w_up, H, D, Q_Q4_0, "w_up.weight");
+        VIEW(ly->w_down, D, H, Q_Q4_0, "w_down.weight");
+    }
+#undef VIEW
+    // RoPE frequencies (+ host cos/sin cache when it fits, as upstream)
+    const uint32_t np = hd / 2;
+    model->rope_freqs = (float*)q_arena_alloc(ctx, np * sizeof(float));
+    if (!model->rope_freqs) return Q_ERR_ARENA_OOM;
+    for (uint32_t i = 0; i < np; ++i)
+        model->rope_freqs[i] = powf(c.rope_freq_base, -2.0f * (float)i / (float)hd);
+    model->rope_cache_enabled = false;
+    model->rope_cos_cache = model->rope_sin_cache = nullptr;
+    if (c.max_seq_len <= 8192) {
+        const size_t cs = (size_t)c.max_seq_len * hd * sizeof(float);
+        model->rope_cos_cache = (float*)q_arena_alloc(ctx, cs);
+        model->rope_sin_cache = (float*)q_arena_alloc(ctx, cs);
+        if (model->rope_cos_cache && model->rope_sin_cache) {
+            for (uint32_t p = 0; p < c.max_seq_len; ++p)
+                for (uint32_t i = 0; i < np; ++i) {
+                    const float th = model->rope_freqs[i] * (float)p;
+                    const size_t o = (size_t)p * hd + 2 * i;
+                    model->rope_cos_cache[o] = model->rope_cos_cache[o + 1] = cosf(th);
+                    model->rope_sin_cache[o] = model->rope_sin_cache[o + 1] = sinf(th);
+                }
+            model->rope_cache_enabled = true;
+        }
+    }
+    ctx->scratch_base_offset = ctx->scratch_head;
+
+    // one-time upload to HBM
+    DevState* s = state_of(ctx, false);
+    if (!s || !s->arena) return Q_ERR_INVALID_ARG;  // q_alloc_arena first (as upstream)
+    q_error_code rc = upload_model(ctx, s, model);
+    if (rc != Q_OK) return rc;
+    if (ctx->kv_buffer) rc = ensure_graphs(ctx, s);
+    return rc;
+}
+
+void llama_free_graph(q_llama_model* model) {
+    if (!model) return;
+    model->token_embd = model->output_norm = model->output = nullptr;
+    model->layers = nullptr;
+    model->ctx = nullptr;
+    memset(&model->config, 0, sizeof model->config);
+}
+
+}  // extern "C"
+
+static size_t kv_bytes_needed(const q_llama_config& c) {
+    return (size_t)c.n_layers * c.n_kv_heads * c.max_seq_len * (c.dim / c.n_heads) * 2 * 4;
+}
+
+static q_error_code ready(q_llama_model* model, q_context* ctx, DevState** out) {
+    DevState* s = state_of(ctx, false);
+    if (!s || !s->built) return Q_ERR_INVALID_ARG;
+    if (ctx->kv_size < kv_bytes_needed(model->config)) return Q_ERR_INVALID_ARG;
+    q_error_code rc = ensure_graphs(ctx, s);
+    if (rc != Q_OK) return rc;
+    *out = s;
+    return Q_OK;
+}
+
+// One graph replay per row: rows 0..seq_len-2 run the layer stack only, the
+// last row also runs the LM head + argmax.  Row t sees the upstream softmax
+// row length N = pos + seq_len and unmasked positions 0..pos+t.
+static q_error_code run_rows(DevState* s, const uint32_t* tokens, uint32_t seq_len, uint32_t pos) {
+    for (uint32_t t = 0; t < seq_len; ++t) {
+        StepParams* hp = &s->h_step[t];
+        hp->token = tokens[t];
+        hp->pos = pos + t;
+        hp->n_row = pos + seq_len;
+        hp->valid = pos + t + 1;
+        Q_CUDA(cudaMemcpyAsync(s->step, hp, sizeof *hp, cudaMemcpyHostToDevice, s->stream));
+        const bool full = t + 1 == seq_len;
+        Q_CUDA(cudaGraphLaunch(full ? s->g_full : s->g_body, s->stream));
+        g_kernel_launches.fetch_add(full ? s->kernels_full : s->kernels_body);
+    }
+    return Q_OK;
+}
+
+extern "C" {
+
+q_error_code llama_forward(q_llama_model* model, q_context* ctx, const uint32_t* tokens,
+                           uint32_t seq_len, uint32_t pos, float* logits) {
+    // upstream model.c:1664-1685
+    if (!model || !ctx || !tokens || !logits) return Q_ERR_INVALID_ARG;
+    if (seq_len == 0) return Q_ERR_INVALID_SIZE;
+    if (seq_len > model->config.max_seq_len) return Q_ERR_INVALID_SIZE;
+    if (pos >= model->config.max_seq_len) return Q_ERR_INVALID_ARG;
+    if (!ctx->scratch_buffer || !ctx->kv_buffer) return Q_ERR_INVALID_ARG;
+    if ((uint64_t)pos + seq_len > model->config.max_seq_len) return Q_ERR_INVALID_ARG;
+    for (uint32_t t = 0; t < seq_len; ++t)
+        if (tokens[t] >= model->config.vocab_size) return Q_ERR_INVALID_ARG;
+    DevState* s = nullptr;
+    q_error_code rc = ready(model, ctx, &s);
+    if (rc != Q_OK) return rc;
+    Q_CUDA(cudaStreamSynchronize(s->stream));  // pinned step slots may still be in use
+    if ((rc = run_rows(s, tokens, seq_len, pos)) != Q_OK) return rc;
+    Q_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)model->config.vocab_size * 4,
+                           cudaMemcpyDeviceToHost, s->stream));
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    return check_device_status("llama_forward");
+}
+
+q_error_code q_sample_token(const float* logits, uint32_t vocab_size, float temperature,
+                            uint32_t top_k, float top_p, uint32_t* token_id_out, q_context* ctx) {
+    (void)top_k;
+    (void)top_p;
+    (void)ctx;
+    if (!logits || !token_id_out) return Q_ERR_INVALID_ARG;
+    if (vocab_size == 0) return Q_ERR_INVALID_SIZE;
+    if (!(temperature >= 0.0f) || !std::isfinite(temperature)) return Q_ERR_INVALID_ARG;
+    if (temperature >= 1e-6f) return Q_ERR_INVALID_ARG;  // stochastic sampling: not in this build
+    // upstream main.c:870-881 on the caller's host logits
+    uint32_t bi = 0;
+    float bv = logits[0];
+    for (uint32_t i = 1; i < vocab_size; ++i)
+        if (logits[i] > bv) {
+            bv = logits[i];
+            bi = i;
+        }
+    *token_id_out = bi;
+    return Q_OK;
+}
+
+q_error_code q_generate(q_generation_state* st) {
+    // upstream main.c:994-1131; the argmax is taken on the device
+    if (!st || !st->ctx || !st->model || !st->tokenizer || !st->prompt_tokens ||
+        !st->generated_tokens)
+        return Q_ERR_INVALID_ARG;
+    if (st->num_prompt_tokens == 0 || st->max_tokens == 0) return Q_ERR_INVALID_SIZE;
+    if (!(st->temperature >= 0.0f) || !std::isfinite(st->temperature)) return Q_ERR_INVALID_ARG;
+    if (!st->tokenizer->initialized) return Q_ERR_INVALID_ARG;
+    if (!st->ctx->scratch_buffer || !st->ctx->kv_buffer) return Q_ERR_INVALID_ARG;
+    if (st->temperature >= 1e-6f) return Q_ERR_INVALID_ARG;  // greedy only in this build
+    const q_llama_config& c = st->model->config;
+    if (st->num_prompt_tokens > c.max_seq_len) return Q_ERR_INVALID_SIZE;
+    for (uint32_t t = 0; t < st->num_prompt_tokens; ++t)
+        if (st->prompt_tokens[t] >= c.vocab_size) return Q_ERR_INVALID_ARG;
+    st->num_generated_tokens = 0;
+    st->current_pos = 0;
+    q_arena_reset(st->ctx);
+    DevState* s = nullptr;
+    q_error_code rc = ready(st->model, st->ctx, &s);
+    if (rc != Q_OK) return rc;
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    if ((rc = run_rows(s, st->prompt_tokens, st->num_prompt_tokens, 0)) != Q_OK) return rc;
+    st->current_pos = st->num_prompt_tokens;
+    while (st->num_generated_tokens < st->max_tokens) {
+        if (st->current_pos >= c.max_seq_len) break;
+        uint32_t tok = 0;
+        Q_CUDA(cudaMemcpyAsync(&tok, s->last_tok, 4, cudaMemcpyDeviceToHost, s->stream));
+        Q_CUDA(cudaStreamSynchronize(s->stream));
+        if ((rc = check_device_status("q_generate")) != Q_OK) return rc;
+        if (tok >= c.vocab_size) return Q_ERR_INVALID_ARG;
+        st->generated_tokens[st->num_generated_tokens++] = tok;
+        if (tok == st->tokenizer->eos_token_id) break;
+        q_arena_reset(st->ctx);
+        if ((rc = run_rows(s, &tok, 1, st->current_pos)) != Q_OK) return rc;
+        st->current_pos++;
+    }
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    return check_device_status("q_generate");
+}
+
+// ---- additive device-resident entry points -------------------------------------
+
+void* q_b200_stream(q_context* ctx) {
+    DevState* s = state_of(ctx, false);
+    return s ? (void*)s->stream : nullptr;
+}
+
+const float* q_b200_device_logits(q_context* ctx) {
+    DevState* s = state_of(ctx, false);
+    return s ? s->logits : nullptr;
+}
+
+q_error_code q_b200_kv_write(q_context* ctx, size_t off, const void* host, size_t bytes) {
+    if (!ctx || !host || !ctx->kv_buffer) return Q_ERR_INVALID_ARG;
+    if (off > ctx->kv_size || bytes > ctx->kv_size - off) return Q_ERR_INVALID_SIZE;
+    if (DevState* s = state_of(ctx, false)) Q_CUDA(cudaStreamSynchronize(s->stream));
+    Q_CUDA(cudaMemcpy((uint8_t*)ctx->kv_buffer + off, host, bytes, cudaMemcpyHostToDevice));
+    return Q_OK;
+}
+
+q_error_code q_b200_kv_read(q_context* ctx, size_t off, void* host, size_t bytes) {
+    if (!ctx || !host || !ctx->kv_buffer) return Q_ERR_INVALID_ARG;
+    if (off > ctx->kv_size || bytes > ctx->kv_size - off) return Q_ERR_INVALID_SIZE;
+    if (DevState* s = state_of(ctx, false)) Q_CUDA(cudaStreamSynchronize(s->stream));
+    Q_CUDA(cudaMemcpy(host, (uint8_t*)ctx->kv_buffer + off, bytes, cudaMemcpyDeviceToHost));
+    return Q_OK;
+}
+
+q_error_code q_b200_decode_loop(q_llama_model* model, q_context* ctx, uint32_t first_token,
+                                uint32_t pos, uint32_t n_steps, uint32_t* out_tokens, int sync) {
+    if (!model || !ctx) return Q_ERR_INVALID_ARG;
+    if (n_steps == 0) return Q_ERR_INVALID_SIZE;
+    if (first_token >= model->config.vocab_size) return Q_ERR_INVALID_ARG;
+    if ((uint64_t)pos + n_steps > model->config.max_seq_len) return Q_ERR_INVALID_ARG;
+    DevState* s = nullptr;
+    q_error_code rc = ready(model, ctx, &s);
+    if (rc != Q_OK) return rc;
+    Q_CUDA(cudaStreamSynchronize(s->stream));  // h_step[0] may still be read by a prior copy
+    StepParams* hp = &s->h_step[0];
+    hp->token = first_token;
+    hp->pos = pos;
+    hp->n_row = hp->valid = pos + 1;
+    Q_CUDA(cudaMemcpyAsync(s->step, hp, sizeof *hp, cudaMemcpyHostToDevice, s->stream));
+    Q_CUDA(cudaMemsetAsync(s->tok_count, 0, 4, s->stream));
+    for (uint32_t i = 0; i < n_steps; ++i) {
+        Q_CUDA(cudaGraphLaunch(s->g_full, s->stream));
+        g_kernel_launches.fetch_add(s->kernels_full);
+    }
+    if (!sync) return Q_OK;
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    if ((rc = check_device_status("q_b200_decode_loop")) != Q_OK) return rc;
+    if (out_tokens) {
+        const uint32_t n = std::min(n_steps, s->tok_cap);
+        Q_CUDA(cudaMemcpy(out_tokens, s->tok_out, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    }
+    return Q_OK;
+}
+
+q_error_code q_b200_decode_greedy(q_llama_model* model, q_context* ctx, uint32_t token,
+                                  uint32_t pos, uint32_t* next_token) {
+    if (!next_token) return Q_ERR_INVALID_ARG;
+    q_error_code rc = q_b200_decode_loop(model, ctx, token, pos, 1, nullptr, 1);
+    if (rc != Q_OK) return rc;
+    DevState* s = state_of(ctx, false);
+    Q_CUDA(cudaMemcpy(next_token, s->last_tok, 4, cudaMemcpyDeviceToHost));
+    return Q_OK;
+}
+
+}  // extern "C"

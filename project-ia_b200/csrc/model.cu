@@ -1,0 +1,347 @@
+// model.cu — one-time model upload to HBM and the captured decode graphs.
+//
+// Upload (stands beside upstream llama_build_graph, model.c:294-673): every
+// Q4_0 projection is repacked into stream tiles; wq|wk|wv become one matrix
+// (one fused QKV launch), w_gate/w_up are row-interleaved (one fused
+// gate-up-SiLU launch).  FP32 embedding / LM head / norms are copied as is.
+// RoPE tables are built on the host exactly as upstream (powf/cosf/sinf in
+// fp32, duplicated pairs, model.c:625-665) and uploaded.
+//
+// Per-token work (upstream llama_forward, model.c:1655-1850) is 6 kernels per
+// layer — QKV(+RMSNorm, RoPE, KV store), attention scores, attention P.V +
+// combine, wo(+residual), gate/up(+RMSNorm, SiLU*up), down(+residual) — plus
+// the LM head(+final norm, argmax) and a step-advance kernel, captured once
+// into CUDA graphs with programmatic dependent launch between kernels.
+#include <cmath>
+#include <cstdlib>
+
+#include "runtime.cuh"
+
+namespace qb200 {
+
+static q_error_code dalloc(DevState* s, void** p, size_t bytes) {
+    if (!cuda_ok(cudaMalloc(p, bytes ? bytes : 16), "cudaMalloc(weights)")) return Q_ERR_ALLOC_FAILED;
+    s->weight_allocs.push_back(*p);
+    return Q_OK;
+}
+
+q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* model) {
+    (void)ctx;
+    free_model(s);
+    const q_llama_config& c = model->config;
+    s->cfg = c;
+    const uint32_t D = c.dim, H = c.hidden_dim, V = c.vocab_size, L = c.n_layers;
+    s->hd = D / c.n_heads;
+    s->kvd = c.n_kv_heads * s->hd;
+    const uint32_t G = c.n_heads / c.n_kv_heads;
+    if (!(s->hd == 32 || s->hd == 64 || s->hd == 128) || G > (uint32_t)ATT_MAXG ||
+        c.n_heads % c.n_kv_heads || c.max_seq_len == 0)
+        return Q_ERR_INVALID_CONFIG;
+    if (!plan_gemv(D + 2 * s->kvd, D, true, s->p_qkv) || !plan_gemv(D, D, false, s->p_wo) ||
+        !plan_gemv(2 * H, D, true, s->p_gu) || !plan_gemv(D, H, false, s->p_down))
+        return Q_ERR_INVALID_CONFIG;
+    cudaStream_t st = s->stream;
+    const size_t nbD = D / 32, nbH = H / 32;
+    const size_t qkv_aos = (size_t)(D + 2 * s->kvd) * nbD * 20;
+    const size_t gu_aos = (size_t)2 * H * nbD * 20;
+    const size_t down_aos = (size_t)D * nbH * 20;
+    const size_t stage_bytes = std::max(qkv_aos, std::max(gu_aos, down_aos));
+    uint8_t* stage = nullptr;
+    if (!cuda_ok(cudaMalloc(&stage, stage_bytes), "cudaMalloc(stage)")) return Q_ERR_ALLOC_FAILED;
+    q_error_code rc = Q_OK;
+    auto h2d = [&](void* dst, const void* src, size_t n) {
+        return cuda_ok(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, st), "upload");
+    };
+    void* p = nullptr;
+    for (uint32_t l = 0; l < L && rc == Q_OK; ++l) {
+        const q_llama_layer& ly = model->layers[l];
+        if ((rc = dalloc(s, &p, s->p_qkv.packed_bytes))) break;
+        s->qkv.push_back((uint8_t*)p);
+        if (!h2d(stage, ly.wq->data, (size_t)D * nbD * 20) ||
+            !h2d(stage + (size_t)D * nbD * 20, ly.wk->data, (size_t)s->kvd * nbD * 20) ||
+            !h2d(stage + (size_t)(D + s->kvd) * nbD * 20, ly.wv->data, (size_t)s->kvd * nbD * 20) ||
+            !cuda_ok(pack_q4(stage, s->p_qkv, 0, s->qkv.back(), st), "pack qkv")) {
+            rc = Q_ERR_INVALID_ARG;
+            break;
+        }
+        if ((rc = dalloc(s, &p, s->p_wo.packed_bytes))) break;
+        s->wo.push_back((uint8_t*)p);
+        if (!h2d(stage, ly.wo->data, (size_t)D * nbD * 20) ||
+            !cuda_ok(pack_q4(stage, s->p_wo, 0, s->wo.back(), st), "pack wo")) {
+            rc = Q_ERR_INVALID_ARG;
+            break;
+        }
+        if ((rc = dalloc(s, &p, s->p_gu.packed_bytes))) break;
+        s->gu.push_back((uint8_t*)p);
+        if (!h2d(stage, ly.w_gate->data, (size_t)H * nbD * 20) ||
+            !h2d(stage + (size_t)H * nbD * 20, ly.w_up->data, (size_t)H * nbD * 20) ||
+            !cuda_ok(pack_q4(stage, s->p_gu, H, s->gu.back(), st), "pack gate/up")) {
+            rc = Q_ERR_INVALID_ARG;
+            break;
+        }
+        if ((rc = dalloc(s, &p, s->p_down.packed_bytes))) break;
+        s->down.push_back((uint8_t*)p);
+        if (!h2d(stage, ly.w_down->data, down_aos) ||
+            !cuda_ok(pack_q4(stage, s->p_down, 0, s->down.back(), st), "pack down")) {
+            rc = Q_ERR_INVALID_ARG;
+            break;
+        }
+    }
+    if (rc == Q_OK) {
+        rc = dalloc(s, &p, (size_t)L * D * 4);
+        s->attn_norm = (float*)p;
+    }
+    if (rc == Q_OK) {
+        rc = dalloc(s, &p, (size_t)L * D * 4);
+        s->ffn_norm = (float*)p;
+    }
+    for (uint32_t l = 0; l < L && rc == Q_OK; ++l)
+        if (!h2d(s->attn_norm + (size_t)l * D, model->layers[l].attn_norm->data, (size_t)D * 4) ||
+            !h2d(s->ffn_norm + (size_t)l * D, model->layers[l].ffn_norm->data, (size_t)D * 4))
+            rc = Q_ERR_INVALID_ARG;
+    if (rc == Q_OK && !(rc = dalloc(s, &p, (size_t)D * 4))) {
+        s->out_norm = (float*)p;
+        if (!h2d(p, model->output_norm->data, (size_t)D * 4)) rc = Q_ERR_INVALID_ARG;
+    }
+    if (rc == Q_OK && !(rc = dalloc(s, &p, (size_t)V * D * 4))) {
+        s->embd = (float*)p;
+        if (!h2d(p, model->token_embd->data, (size_t)V * D * 4)) rc = Q_ERR_INVALID_ARG;
+    }
+    if (rc == Q_OK && !(rc = dalloc(s, &p, (size_t)V * D * 4))) {
+        s->out_w = (float*)p;
+        if (!h2d(p, model->output->data, (size_t)V * D * 4)) rc = Q_ERR_INVALID_ARG;
+    }
+    // RoPE tables, host-built like upstream model.c:625-665
+    const size_t tab = (size_t)c.max_seq_len * s->hd;
+    std::vector<float> ct(tab), stb(tab);
+    {
+        const uint32_t np = s->hd / 2;
+        std::vector<float> fr(np);
+        for (uint32_t i = 0; i < np; ++i) fr[i] = powf(c.rope_freq_base, -2.0f * (float)i / (float)s->hd);
+        for (uint32_t ps = 0; ps < c.max_seq_len; ++ps)
+            for (uint32_t i = 0; i < np; ++i) {
+                const float th = fr[i] * (float)ps;
+                const float cv = cosf(th), sv = sinf(th);
+                const size_t o = (size_t)ps * s->hd + 2 * i;
+                ct[o] = ct[o + 1] = cv;
+                stb[o] = stb[o + 1] = sv;
+            }
+    }
+    if (rc == Q_OK && !(rc = dalloc(s, &p, tab * 4))) {
+        s->rope_cos = (float*)p;
+        if (!h2d(p, ct.data(), tab * 4)) rc = Q_ERR_INVALID_ARG;
+    }
+    if (rc == Q_OK && !(rc = dalloc(s, &p, tab * 4))) {
+        s->rope_sin = (float*)p;
+        if (!h2d(p, stb.data(), tab * 4)) rc = Q_ERR_INVALID_ARG;
+    }
+    if (rc == Q_OK && !cuda_ok(cudaStreamSynchronize(st), "upload sync")) rc = Q_ERR_INVALID_ARG;
+    cudaFree(stage);
+    if (rc != Q_OK) {
+        free_model(s);
+        return rc;
+    }
+
+    // activations: carved from the device arena once; the watermark moves
+    // past them so per-token work allocates nothing
+    s->arena_head = 0;
+    s->n_chunks = (c.max_seq_len + ATT_CH - 1) / ATT_CH;
+    s->tok_cap = c.max_seq_len;
+    const uint32_t nh = c.n_heads;
+    s->x = (float*)dev_arena_alloc(s, (size_t)D * 4);
+    s->q = (float*)dev_arena_alloc(s, (size_t)D * 4);
+    s->att = (float*)dev_arena_alloc(s, (size_t)D * 4);
+    s->h = (float*)dev_arena_alloc(s, (size_t)H * 4);
+    s->scores = (float*)dev_arena_alloc(s, (size_t)nh * c.max_seq_len * 4);
+    s->cmax = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * 4);
+    s->opart = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * s->hd * 4);
+    s->lpart = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * 4);
+    s->logits = (float*)dev_arena_alloc(s, (size_t)V * 4);
+    s->ticket = (uint32_t*)dev_arena_alloc(s, (size_t)c.n_kv_heads * 4);
+    s->best = (unsigned long long*)dev_arena_alloc(s, 8);
+    s->step = (StepParams*)dev_arena_alloc(s, sizeof(StepParams));
+    s->tok_out = (uint32_t*)dev_arena_alloc(s, (size_t)s->tok_cap * 4);
+    s->tok_count = (uint32_t*)dev_arena_alloc(s, 4);
+    s->last_tok = (uint32_t*)dev_arena_alloc(s, 4);
+    if (!s->x || !s->q || !s->att || !s->h || !s->scores || !s->cmax || !s->opart || !s->lpart ||
+        !s->logits || !s->ticket || !s->best || !s->step || !s->tok_out || !s->tok_count ||
+        !s->last_tok) {
+        free_model(s);
+        return Q_ERR_ARENA_OOM;
+    }
+    s->arena_base = s->arena_head;
+    if (!cuda_ok(cudaMemsetAsync(s->ticket, 0, (size_t)c.n_kv_heads * 4, st), "init") ||
+        !cuda_ok(cudaMemsetAsync(s->best, 0, 8, st), "init") ||
+        !cuda_ok(cudaMemsetAsync(s->tok_count, 0, 4, st), "init") ||
+        !cuda_ok(cudaStreamSynchronize(st), "init sync")) {
+        free_model(s);
+        return Q_ERR_INVALID_ARG;
+    }
+    if (s->h_step) cudaFreeHost(s->h_step);
+    s->h_step = nullptr;
+    if (!cuda_ok(cudaMallocHost(&s->h_step, sizeof(StepParams) * (size_t)c.max_seq_len), "pinned")) {
+        free_model(s);
+        return Q_ERR_ALLOC_FAILED;
+    }
+    s->built = true;
+    return Q_OK;
+}
+
+// ---- graph capture ------------------------------------------------------------------
+
+static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStream_t st) {
+    AttnArgs a{};
+    a.q = s->q;
+    a.kv_layer = kv_layer;
+    a.scores = s->scores;
+    a.cmax = s->cmax;
+    a.opart = s->opart;
+    a.lpart = s->lpart;
+    a.ticket = s->ticket;
+    a.out = s->att;
+    a.step = s->step;
+    a.n_heads = s->cfg.n_heads;
+    a.n_kv_heads = s->cfg.n_kv_heads;
+    a.max_seq = s->cfg.max_seq_len;
+    a.n_chunks = s->n_chunks;
+    a.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
+    const dim3 grid(s->cfg.n_kv_heads, s->n_chunks);
+    cudaError_t e;
+    switch (s->hd) {
+        case 32:
+            e = launch_ex(attn_scores_kernel<32>, grid, dim3(ATT_THREADS), 0, st, true, a);
+            if (e == cudaSuccess) e = launch_ex(attn_pv_kernel<32>, grid, dim3(ATT_THREADS), 0, st, true, a);
+            return e;
+        case 64:
+            e = launch_ex(attn_scores_kernel<64>, grid, dim3(ATT_THREADS), 0, st, true, a);
+            if (e == cudaSuccess) e = launch_ex(attn_pv_kernel<64>, grid, dim3(ATT_THREADS), 0, st, true, a);
+            return e;
+        default:
+            e = launch_ex(attn_scores_kernel<128>, grid, dim3(ATT_THREADS), 0, st, true, a);
+            if (e == cudaSuccess) e = launch_ex(attn_pv_kernel<128>, grid, dim3(ATT_THREADS), 0, st, true, a);
+            return e;
+    }
+}
+
+static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
+    const q_llama_config& c = s->cfg;
+    const uint32_t D = c.dim;
+    const size_t layer_floats = (size_t)c.n_kv_heads * c.max_seq_len * 2 * s->hd;
+    cudaError_t e = cudaSuccess;
+    for (uint32_t l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
+        float* kvl = kv + (size_t)l * layer_floats;
+        GemvArgs g{};
+        g.w = s->qkv[l];
+        g.step = s->step;
+        g.gather = l == 0;
+        g.x = l == 0 ? s->embd : s->x;
+        g.x_copy = l == 0 ? s->x : nullptr;
+        g.norm_w = s->attn_norm + (size_t)l * D;
+        g.eps = c.rms_norm_eps;
+        g.y = s->q;
+        g.epi = EPI_QKV;
+        g.rope_cos = s->rope_cos;
+        g.rope_sin = s->rope_sin;
+        g.kv_layer = kvl;
+        g.hd = s->hd;
+        g.q_rows = D;
+        g.kv_rows = s->kvd;
+        g.max_seq = c.max_seq_len;
+        e = launch_gemv(s->p_qkv, g, st, l != 0);
+        if (e == cudaSuccess) e = enqueue_attention(s, kvl, st);
+        if (e != cudaSuccess) break;
+        GemvArgs o{};
+        o.w = s->wo[l];
+        o.step = s->step;
+        o.x = s->att;
+        o.y = s->x;
+        o.resid = s->x;
+        o.epi = EPI_RESID;
+        e = launch_gemv(s->p_wo, o, st, true);
+        if (e != cudaSuccess) break;
+        GemvArgs u{};
+        u.w = s->gu[l];
+        u.step = s->step;
+        u.x = s->x;
+        u.norm_w = s->ffn_norm + (size_t)l * D;
+        u.eps = c.rms_norm_eps;
+        u.y = s->h;
+        u.epi = EPI_SILU;
+        e = launch_gemv(s->p_gu, u, st, true);
+        if (e != cudaSuccess) break;
+        GemvArgs d{};
+        d.w = s->down[l];
+        d.step = s->step;
+        d.x = s->h;
+        d.y = s->x;
+        d.resid = s->x;
+        d.epi = EPI_RESID;
+        e = launch_gemv(s->p_down, d, st, true);
+    }
+    return e;
+}
+
+static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
+    HeadArgs h{};
+    h.w = s->out_w;
+    h.x = s->x;
+    h.norm_w = s->out_norm;
+    h.eps = s->cfg.rms_norm_eps;
+    h.rows = s->cfg.vocab_size;
+    h.K = s->cfg.dim;
+    h.row_base = 0;
+    h.logits = s->logits;
+    h.best = s->best;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    });
+    const uint32_t grid = std::max<uint32_t>(
+        1, std::min<uint32_t>(2 * device_sms(), (s->cfg.vocab_size + 15) / 16));
+    cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS),
+                              (size_t)s->cfg.dim * 4, st, true, h);
+    if (e != cudaSuccess) return e;
+    AdvanceArgs a{};
+    a.step = s->step;
+    a.best = s->best;
+    a.token_out = s->tok_out;
+    a.token_count = s->tok_count;
+    a.token_cap = s->tok_cap;
+    a.last_token = s->last_tok;
+    return launch_ex(advance_kernel, dim3(1), dim3(32), 0, st, true, a);
+}
+
+static q_error_code capture(DevState* s, float* kv, bool with_head, cudaGraphExec_t* out,
+                            uint64_t* n_kernels) {
+    cudaStream_t st = s->stream;
+    cudaGraph_t g = nullptr;
+    const uint64_t before = g_kernel_launches.load();
+    if (!cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture"))
+        return Q_ERR_INVALID_ARG;
+    cudaError_t e = enqueue_layers(s, kv, st);
+    if (e == cudaSuccess && with_head) e = enqueue_head(s, st);
+    cudaError_t e2 = cudaStreamEndCapture(st, &g);
+    *n_kernels = g_kernel_launches.load() - before;
+    g_kernel_launches.fetch_sub(*n_kernels);  // captured, not launched
+    if (!cuda_ok(e, "capture launches") || !cuda_ok(e2, "end capture")) {
+        if (g) cudaGraphDestroy(g);
+        return Q_ERR_INVALID_ARG;
+    }
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return cuda_ok(e, "graph instantiate") ? Q_OK : Q_ERR_INVALID_ARG;
+}
+
+q_error_code ensure_graphs(q_context* ctx, DevState* s) {
+    if (s->g_full && s->graph_kv == ctx->kv_buffer) return Q_OK;
+    if (s->g_body) cudaGraphExecDestroy(s->g_body);
+    if (s->g_full) cudaGraphExecDestroy(s->g_full);
+    s->g_body = s->g_full = nullptr;
+    float* kv = (float*)ctx->kv_buffer;
+    q_error_code rc = capture(s, kv, false, &s->g_body, &s->kernels_body);
+    if (rc == Q_OK) rc = capture(s, kv, true, &s->g_full, &s->kernels_full);
+    if (rc == Q_OK) s->graph_kv = ctx->kv_buffer;
+    return rc;
+}
+
+}  // namespace qb200
