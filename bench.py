@@ -1,0 +1,334 @@
+#!/usr/bin/env python3
+"""Benchmark: Llama-3-8B-shaped Q4_0 batch-1 greedy decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: 32 layers, dim 4096, 32 query / 8 KV
+heads (head_dim 128), FFN 14336, vocab 128256, random-init Q4_0 weights
+(FP32 embedding / LM head), KV cache pre-filled with 2048 positions of
+N(0,1), then greedy decode.  A step is one decoded token.  Synthetic data
+from the library's counter-based generators; the per-token stream (7 GB of
+weights + LM head + KV) is ~55x the 126 MB L2, so no L2 flush is needed.
+
+`value` times K device-resident decode steps (the captured per-token CUDA
+graph replayed, the argmax fed back on the device) with CUDA events on the
+library's stream.  `e2e` times K calls of the upstream entry point
+llama_forward (host token in, host logits out, so each step copies the token
+and step scalars H2D and 513 KB of logits D2H).  With --gpus N each rank
+decodes its own sequence on its own GPU (replicas; weak scaling).
+
+--impl reference times the upstream CPU implementation of the same path:
+the upstream AVX2 kernels (compiled from the upstream sources into
+oracle/_ref) composed into the same graph, all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "project-ia_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+METRIC = "Llama-3-8B Q4_0 decode tok/s"
+CFG8B = dict(vocab=128256, dim=4096, hidden=14336, layers=32, heads=32, kv_heads=8)
+PREFILL = 2048
+SEED = 0
+
+
+def q4_linear_bytes(c) -> int:
+    D, H = c["dim"], c["hidden"]
+    kvd = c["kv_heads"] * (D // c["heads"])
+    per_layer = (D * D * 2 + kvd * D * 2 + H * D * 3) * 5 // 8  # 0.625 B / weight
+    return per_layer * c["layers"]
+
+
+def token_bytes(c, ctx_len: int) -> int:
+    """Algorithmic HBM bytes of one decode token at context length ctx_len."""
+    D = c["dim"]
+    hd = D // c["heads"]
+    lm_head = c["vocab"] * D * 4
+    kv = c["layers"] * c["kv_heads"] * ctx_len * hd * 2 * 4
+    small = D * 4 * (1 + 2 * c["layers"] + 1)  # embedding row, norm gains, final norm
+    return q4_linear_bytes(c) + lm_head + kv + small
+
+
+def model_path(max_seq: int) -> str:
+    d = Path(os.environ.get("QORUS_TMPDIR", "/dev/shm" if Path("/dev/shm").exists() else "/tmp"))
+    return str(d / f"qorus_llama3_8b_q4_{max_seq}_s{SEED}.qorus")
+
+
+def ensure_model(Q, max_seq: int, rank: int, barrier) -> tuple[str, object]:
+    cfg = Q.config(CFG8B["vocab"], CFG8B["dim"], CFG8B["hidden"], CFG8B["layers"],
+                   CFG8B["heads"], CFG8B["kv_heads"], max_seq)
+    path = model_path(max_seq)
+    size = int(Q.lib.q_b200_model_file_size(C.byref(cfg)))
+    if rank == 0 and not (Path(path).exists() and Path(path).stat().st_size == size):
+        Q.write_model(path, cfg, seed=SEED, threads=0)
+    barrier()
+    return path, cfg
+
+
+def kv_image(Q, cfg) -> np.ndarray:
+    hd = cfg.dim // cfg.n_heads
+    kv = np.zeros(cfg.n_layers * cfg.n_kv_heads * cfg.max_seq_len * 2 * hd, np.float32)
+    Q.check(Q.lib.q_b200_fill_kv_prefill(Q.ptr(kv), C.byref(cfg), PREFILL, SEED + 1, 0), "kv")
+    return kv
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
+    """Dominant kernel: the fused gate/up Q4_0 GEMV shape of the 8B layer
+    (28672 x 4096), launched back to back over 4 distinct weight sets (294 MB
+    > L2) on torch's stream and timed with CUDA events."""
+    M, K, n_sets, iters = 2 * CFG8B["hidden"], CFG8B["dim"], 4, 64
+    nblk = M * K // 32
+    packed = []
+    host = np.zeros(nblk * 20, np.uint8)
+    for i in range(n_sets):
+        Q.lib.q_b200_fill_q4(Q.ptr(host), nblk, SEED + 10 + i, 3, 0, 0.001, 0.01, 0)
+        src = torch.from_numpy(host).cuda()
+        dst = torch.empty(Q.lib.q_b200_q4_packed_bytes(M, K), dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        Q.check(Q.lib.q_b200_q4_pack(src.data_ptr(), M, K, dst.data_ptr(), None), "pack")
+        torch.cuda.synchronize()
+        packed.append(dst)
+        del src
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(M, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(8):
+        Q.check(Q.lib.q_b200_gemv_q4(packed[i % n_sets].data_ptr(), M, K, x.data_ptr(), y.data_ptr(), s), "gemv")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        Q.lib.q_b200_gemv_q4(packed[i % n_sets].data_ptr(), M, K, x.data_ptr(), y.data_ptr(), s)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    bytes_launch = M * K * 5 // 8 + 4 * K + 4 * M
+    achieved = bytes_launch / (us * 1e-6) / 1e9
+    return {"kernel": "gemv_q4_kernel (fused gate/up 28672x4096)", "bound": "hbm",
+            "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "us_per_launch": round(us, 2),
+            "bytes_per_launch": bytes_launch, "traffic": None, "peak_source": "of measured"}
+
+
+def cpu_reference_decode(path: str, cfg, steps: int, threads: int):
+    """Upstream AVX2 kernels (oracle/_ref) over the same model and KV image."""
+    import oracle as O
+    kind = "reference"
+    try:
+        m = O.RefModel(path, threads=threads)
+    except (RuntimeError, OSError):
+        m = O.OracleModel(path, threads=threads)
+        kind = "port"
+    m.kv[:] = kv_image(__import__("qorus_b200"), cfg)
+    tok = 1
+    times = []
+    for i in range(steps):
+        t0 = time.perf_counter()
+        lg = m.forward(np.array([tok], np.uint32), PREFILL + i)
+        times.append(time.perf_counter() - t0)
+        tok = int(np.argmax(lg))
+    m.close()
+    return kind, times
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    max_seq = PREFILL + 2 * (args.steps + args.warmup) + 64
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import qorus_b200 as Q
+        path, cfg = ensure_model(Q, max_seq, 0, lambda: None)
+        threads = os.cpu_count() or 1
+        n = max(1, min(args.steps, 16))
+        kind, times = cpu_reference_decode(path, cfg, args.warmup // 3 + n, threads)
+        times = times[args.warmup // 3:]
+        tps = len(times) / sum(times)
+        line = {"metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "impl": "reference",
+                "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup // 3,
+                "ms_per_step": round(1e3 * sum(times) / len(times), 2), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32 (q4_0 weights)",
+                "data": "synthetic", "config": {"workload": "llama3-8b-q4_0 decode, batch 1, "
+                                                "kv prefill 2048", "prefill": PREFILL},
+                "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads,
+                                 "kind": kind, "sample": f"{len(times)} decode steps of the "
+                                 "8B-shaped model at context 2049+ (every step a full token)"},
+                "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    import qorus_b200 as Q
+    path, cfg = ensure_model(Q, max_seq, rank, barrier)
+    t_load = time.perf_counter()
+    m = Q.Model(path)
+    kv = kv_image(Q, cfg)
+    m.kv_write(kv)
+    del kv
+    t_load = time.perf_counter() - t_load
+    stream = torch.cuda.ExternalStream(m.stream)
+
+    # warm-up: W device steps
+    pos = PREFILL
+    m.decode_loop(1, pos, args.warmup, sync=True)
+    pos += args.warmup
+    launches0 = Q.lib.q_b200_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        Q.check(Q.lib.q_b200_decode_loop(C.byref(m.model), C.byref(m.ctx), 1, pos, args.steps,
+                                         None, 0), "decode_loop")
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = Q.lib.q_b200_kernel_launches() - launches0
+    pos += args.steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * args.steps / (ms * 1e-3)
+
+    # e2e: the upstream entry point, host token in / host logits out
+    tok = np.array([1], np.uint32)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        lg = m.forward(tok, pos + i)
+        tok[0] = int(np.argmax(lg))
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * args.steps / e2e_s
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    roof = gemv_roofline(Q, torch, peak)
+    if not peaks:
+        roof["peak_source"] = "of fallback"
+    ctx_mid = PREFILL + args.warmup + args.steps // 2
+    step_bytes = token_bytes(CFG8B, ctx_mid)
+    step_gbs = step_bytes / (ms * 1e-3 / args.steps) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        m.close()
+        threads = os.cpu_count() or 1
+        kind, times = cpu_reference_decode(path, cfg, 3, threads)
+        cpu = {"value": round(len(times) / sum(times), 3), "unit": "tok/s", "cores": threads,
+               "kind": kind, "sample": f"{len(times)} full decode steps of the same 8B-shaped "
+               "model and KV image (upstream AVX2 kernels, row-parallel over host threads)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (q4_0 weights)", "data": "synthetic",
+            "config": {"workload": "llama3-8b-q4_0 decode, batch 1, kv prefill 2048 (BASELINE configs[2])",
+                       "layers": 32, "dim": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
+                       "global_batch": world, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (7 GB streamed per token)"},
+            "roofline": roof,
+            "step_roofline": {"bytes_per_token": step_bytes, "achieved": round(step_gbs, 1),
+                              "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 16,
+                    "d2h_bytes_per_step": CFG8B["vocab"] * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "load_s": round(t_load, 1),
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
