@@ -196,6 +196,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["gemv"], help="time one kernel alone (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -230,6 +231,10 @@ def main():
 
     import torch
     torch.cuda.set_device(local)
+    if args.only == "gemv":
+        import qorus_b200 as Q
+        print(json.dumps(gemv_roofline(Q, torch, 6450.9)), flush=True)
+        return
     dist = None
     if world > 1:
         import torch.distributed as dist
