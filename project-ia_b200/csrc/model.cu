@@ -145,7 +145,10 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     // activations: carved from the device arena once; the watermark moves
     // past them so per-token work allocates nothing
     s->arena_head = 0;
-    s->n_chunks = (c.max_seq_len + ATT_CH - 1) / ATT_CH;
+    // attention CTAs per KV head: all (n_kv x NC) must be co-resident (2 per SM)
+    s->n_chunks = std::max<uint32_t>(1, std::min<uint32_t>(
+        2u * (uint32_t)device_sms() / c.n_kv_heads,
+        (c.max_seq_len + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK));
     s->tok_cap = c.max_seq_len;
     const uint32_t nh = c.n_heads;
     s->x = (float*)dev_arena_alloc(s, (size_t)D * 4);
@@ -157,7 +160,7 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     s->opart = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * s->hd * 4);
     s->lpart = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * 4);
     s->logits = (float*)dev_arena_alloc(s, (size_t)V * 4);
-    s->ticket = (uint32_t*)dev_arena_alloc(s, (size_t)c.n_kv_heads * 4);
+    s->ticket = (uint32_t*)dev_arena_alloc(s, (size_t)c.n_kv_heads * 16);
     s->best = (unsigned long long*)dev_arena_alloc(s, 8);
     s->step = (StepParams*)dev_arena_alloc(s, sizeof(StepParams));
     s->tok_out = (uint32_t*)dev_arena_alloc(s, (size_t)s->tok_cap * 4);
@@ -170,7 +173,7 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
         return Q_ERR_ARENA_OOM;
     }
     s->arena_base = s->arena_head;
-    if (!cuda_ok(cudaMemsetAsync(s->ticket, 0, (size_t)c.n_kv_heads * 4, st), "init") ||
+    if (!cuda_ok(cudaMemsetAsync(s->ticket, 0, (size_t)c.n_kv_heads * 16, st), "init") ||
         !cuda_ok(cudaMemsetAsync(s->best, 0, 8, st), "init") ||
         !cuda_ok(cudaMemsetAsync(s->tok_count, 0, 4, st), "init") ||
         !cuda_ok(cudaStreamSynchronize(st), "init sync")) {
@@ -197,7 +200,7 @@ static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStr
     a.cmax = s->cmax;
     a.opart = s->opart;
     a.lpart = s->lpart;
-    a.ticket = s->ticket;
+    a.sync = s->ticket;
     a.out = s->att;
     a.step = s->step;
     a.n_heads = s->cfg.n_heads;
@@ -205,21 +208,23 @@ static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStr
     a.max_seq = s->cfg.max_seq_len;
     a.n_chunks = s->n_chunks;
     a.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
-    const dim3 grid(s->cfg.n_kv_heads, s->n_chunks);
-    cudaError_t e;
+    // cooperative: every CTA of the grid is resident, so the per-head
+    // barriers inside the kernel cannot wait on an unscheduled CTA; no
+    // programmatic overlap with the QKV GEMV before it for the same reason
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s->cfg.n_kv_heads, s->n_chunks);
+    cfg.blockDim = dim3(ATT_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     switch (s->hd) {
-        case 32:
-            e = launch_ex(attn_scores_kernel<32>, grid, dim3(ATT_THREADS), 0, st, true, a);
-            if (e == cudaSuccess) e = launch_ex(attn_pv_kernel<32>, grid, dim3(ATT_THREADS), 0, st, true, a);
-            return e;
-        case 64:
-            e = launch_ex(attn_scores_kernel<64>, grid, dim3(ATT_THREADS), 0, st, true, a);
-            if (e == cudaSuccess) e = launch_ex(attn_pv_kernel<64>, grid, dim3(ATT_THREADS), 0, st, true, a);
-            return e;
-        default:
-            e = launch_ex(attn_scores_kernel<128>, grid, dim3(ATT_THREADS), 0, st, true, a);
-            if (e == cudaSuccess) e = launch_ex(attn_pv_kernel<128>, grid, dim3(ATT_THREADS), 0, st, true, a);
-            return e;
+        case 32: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<32>, a);
+        case 64: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, a);
+        default: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, a);
     }
 }
 

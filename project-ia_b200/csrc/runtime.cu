@@ -82,13 +82,15 @@ bool plan_gemv(uint32_t M, uint32_t K, bool pairs, GemvPlan& p) {
         }
     }
     if (!bpt) return false;
+    if (R / c > 4) R = 4 * c;  // kernels are instantiated for 1, 2 or 4 rows per thread
+    if ((R * nb) % 4) return false;
     p.M = M;
     p.K = K;
     p.R = R;
     p.c = c;
     p.bpt = bpt;
     p.n_tiles = (M + R - 1) / R;
-    p.grid = std::min<uint32_t>(p.n_tiles, (uint32_t)device_sms());
+    p.grid = std::min<uint32_t>(p.n_tiles, 2u * (uint32_t)device_sms());  // 2 CTAs per SM
     p.threads = nb / bpt * c + 32;
     p.smem = gemv_smem_bytes(R, K, bpt);
     p.packed_bytes = (size_t)p.n_tiles * gemv_tile_bytes(R, K);
@@ -102,14 +104,20 @@ cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, cudaStream_t s, bool pdl)
     a.c = p.c;
     a.bpt = p.bpt;
     a.n_tiles = p.n_tiles;
+    using Kern = void (*)(GemvArgs);
+    static const Kern table[2][3] = {
+        {gemv_q4_kernel<1, 1>, gemv_q4_kernel<1, 2>, gemv_q4_kernel<1, 4>},
+        {gemv_q4_kernel<2, 1>, gemv_q4_kernel<2, 2>, gemv_q4_kernel<2, 4>}};
     static std::once_flag once;
     std::call_once(once, [] {
-        cudaFuncSetAttribute(gemv_q4_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(gemv_q4_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        for (auto& row : table)
+            for (Kern k : row)
+                cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     });
-    if (p.bpt == 1)
-        return launch_ex(gemv_q4_kernel<1>, dim3(p.grid), dim3(p.threads), p.smem, s, pdl, a);
-    return launch_ex(gemv_q4_kernel<2>, dim3(p.grid), dim3(p.threads), p.smem, s, pdl, a);
+    const uint32_t rows = p.R / p.c;
+    const int ri = rows == 1 ? 0 : rows == 2 ? 1 : rows == 4 ? 2 : -1;
+    if (ri < 0 || (p.bpt != 1 && p.bpt != 2)) return cudaErrorInvalidValue;
+    return launch_ex(table[p.bpt - 1][ri], dim3(p.grid), dim3(p.threads), p.smem, s, pdl, a);
 }
 
 cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,
