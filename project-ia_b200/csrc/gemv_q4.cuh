@@ -160,7 +160,6 @@ __global__ void __launch_bounds__(GEMV_MAX_CONSUMERS + 32, 2) gemv_q4_kernel(con
         for (uint32_t i = tid; i < a.K; i += T) a.x_copy[i] = xs[i];
 
     float2 xr[BPT][16];
-    float nx136[BPT];  // -136 * sum of the block's 32 inputs (see the dequant note below)
 #pragma unroll
     for (int bi = 0; bi < BPT; ++bi) {
         const uint32_t b = cb + bi * nbc;
@@ -180,22 +179,18 @@ __global__ void __launch_bounds__(GEMV_MAX_CONSUMERS + 32, 2) gemv_q4_kernel(con
             xr[bi][2 * i] = make_float2(v.x, v.y);
             xr[bi][2 * i + 1] = make_float2(v.z, v.w);
         }
-        float sx = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sx += xr[bi][i].x + xr[bi][i].y;
-        nx136[bi] = -136.0f * sx;
     }
 
     const bool pairs = (a.epi == EPI_QKV || a.epi == EPI_SILU);
     const uint32_t units = pairs ? a.R / 2 : a.R;
 
     // Dequantisation: one PRMT moves a nibble (pre-masked into the low half
-    // of a byte) into bits 16..19 under the exponent byte 0x3F, giving the
-    // float d = 0.5 + q/256 exactly.  Then sum_j d_j x_j = X/2 + (sum q x)/256
-    // (X = block input sum), so sum (q - 8) x = 256*dot - 136*X.  The X/2
-    // term cancels against a value ~10x smaller at most, costing ~4 bits of
-    // the fp32 accumulator (relative error ~1e-6 per block), and saves the
-    // exact-subtract instruction per weight pair.
+    // of a byte) under the exponent byte 0x4B, giving the float 2^23 + q; a
+    // packed subtract of 2^23 + 8 then yields q - 8 exactly.  (Folding the
+    // -8 into a block-sum correction instead saves that subtract but costs
+    // ~4 bits through cancellation, which long-context attention amplified
+    // past the parity tolerance.)
+    const float2 bias = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
     for (uint32_t k = 0; k < n_my; ++k) {
         const uint32_t s = k % GEMV_NSTAGE;
         const bool ok = mbar_wait(&full[s], (k / GEMV_NSTAGE) & 1, QDEV_WAIT_FULL_TIMEOUT);
@@ -220,16 +215,17 @@ __global__ void __launch_bounds__(GEMV_MAX_CONSUMERS + 32, 2) gemv_q4_kernel(con
                     const uint32_t hi = (words[wi] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
                     for (int m = 0; m < 4; ++m) {
-                        const uint32_t sel = 0x7054u | ((uint32_t)m << 8);
-                        const float2 d = make_float2(__uint_as_float(prmt(lo, 0x3F000000u, sel)),
-                                                     __uint_as_float(prmt(hi, 0x3F000000u, sel)));
+                        const uint32_t sel = 0x7540u | (uint32_t)m;
+                        float2 d = make_float2(__uint_as_float(prmt(lo, 0x4B000000u, sel)),
+                                               __uint_as_float(prmt(hi, 0x4B000000u, sel)));
+                        d = __fadd2_rn(d, bias);  // exactly q - 8
                         if (m & 1) acc1 = __ffma2_rn(d, xr[bi][4 * wi + m], acc1);
                         else acc0 = __ffma2_rn(d, xr[bi][4 * wi + m], acc0);
                     }
                 }
                 const float dot =
                     __fadd_rn(__fadd_rn(acc0.x, acc0.y), __fadd_rn(acc1.x, acc1.y));
-                part = __fmaf_rn(scale, __fmaf_rn(256.0f, dot, nx136[bi]), part);
+                part = __fmaf_rn(scale, dot, part);
             }
             rb[r * nbc + cb] = ok ? part : 0.0f;
         }
