@@ -49,14 +49,14 @@ extern "C" {
 
 size_t q_b200_q4_packed_bytes(uint32_t M, uint32_t K) {
     GemvPlan p;
-    return plan_gemv(M, K, false, p) ? p.packed_bytes : 0;
+    return plan_gemv(M, K, p) ? p.packed_bytes : 0;
 }
 
 q_error_code q_b200_q4_pack(const q_block_q4_0* d_src, uint32_t M, uint32_t K, void* d_dst,
                             void* stream) {
     if (!d_src || !d_dst) return Q_ERR_INVALID_ARG;
     GemvPlan p;
-    if (!plan_gemv(M, K, false, p)) return Q_ERR_INVALID_SIZE;
+    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
     Q_CUDA(pack_q4((const uint8_t*)d_src, p, 0, (uint8_t*)d_dst, (cudaStream_t)stream));
     return Q_OK;
 }
@@ -67,13 +67,13 @@ q_error_code q_b200_gemv_q4(const void* d_packed, uint32_t M, uint32_t K, const 
     if (d_x == d_y) return Q_ERR_ALIASING;
     if (((uintptr_t)d_x & 15) || ((uintptr_t)d_packed & 15)) return Q_ERR_MISALIGNED;
     GemvPlan p;
-    if (!plan_gemv(M, K, false, p)) return Q_ERR_INVALID_SIZE;
+    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
     GemvArgs a{};
     a.w = (const uint8_t*)d_packed;
     a.x = d_x;
     a.y = d_y;
     a.epi = EPI_STORE;
-    Q_CUDA(launch_gemv(p, a, (cudaStream_t)stream, false));
+    Q_CUDA(launch_gemv(p, a, op_gemv_scratch(p), (cudaStream_t)stream, false));
     return Q_OK;
 }
 
@@ -90,7 +90,7 @@ q_error_code q_gemv_q4_f32_avx2(const q_tensor* w, const float* x, float* y) {
     if (w->nb[0] != (size_t)nb * sizeof(q_block_q4_0)) return Q_ERR_INVALID_ARG;
     if (!w->data) return Q_ERR_INVALID_ARG;
     GemvPlan p;
-    if (!plan_gemv(M, K, false, p)) return Q_ERR_INVALID_SIZE;
+    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
     DevBuf aos, packed, dx, dy;
     q_error_code rc;
     if ((rc = to_dev(aos, w->data, (size_t)M * nb * 20)) || (rc = to_dev(dx, x, (size_t)K * 4)))
@@ -102,7 +102,7 @@ q_error_code q_gemv_q4_f32_avx2(const q_tensor* w, const float* x, float* y) {
     a.x = dx.f();
     a.y = dy.f();
     a.epi = EPI_STORE;
-    Q_CUDA(launch_gemv(p, a, op_stream(), false));
+    Q_CUDA(launch_gemv(p, a, op_gemv_scratch(p), op_stream(), false));
     return finish(y, dy.p, (size_t)M * 4);
 }
 

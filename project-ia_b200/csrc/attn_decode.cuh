@@ -213,19 +213,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
     head_barrier(ctr + 1, n_act);
 
     // ---- phase 3: this CTA's slice of the outputs --------------------------------
+    // The partials sit in L2; the chunk sums are spread over lanes so every
+    // load of a warp is in flight at once (a serial loop over chunks is a
+    // chain of L2 round trips).
     {
+        if (warp < G) {  // softmax denominators
+            float l = 0.0f;
+            for (uint32_t k = lane; k < n_act; k += 32)
+                l += __ldcg(&a.lpart[(size_t)(h * G + warp) * a.n_chunks + k]);
+            l = warp_sum(l);
+            if (lane == 0) gmax[warp] = __fdiv_rn(1.0f, l);  // gmax now holds 1/L
+        }
+        __syncthreads();
         const uint32_t total = G * HD;
         const uint32_t per = (total + n_act - 1) / n_act;
         const uint32_t o0 = c * per, o1 = min(o0 + per, total);
-        for (uint32_t i = o0 + tid; i < o1; i += ATT_THREADS) {
-            const uint32_t g = i / HD, d = i % HD;
-            const size_t row = (size_t)(h * G + g) * a.n_chunks;
-            float l = 0.0f, s = 0.0f;
-            for (uint32_t k = 0; k < n_act; ++k) {
-                l += __ldcg(&a.lpart[row + k]);
-                s += __ldcg(&a.opart[(row + k) * HD + d]);
+        if (n_act <= 8) {
+            for (uint32_t i = o0 + tid; i < o1; i += ATT_THREADS) {
+                const uint32_t g = i / HD, d = i % HD;
+                const size_t row = (size_t)(h * G + g) * a.n_chunks;
+                float s = 0.0f;
+#pragma unroll 8
+                for (uint32_t k = 0; k < n_act; ++k) s += __ldcg(&a.opart[(row + k) * HD + d]);
+                a.out[(size_t)(h * G + g) * HD + d] = __fmul_rn(s, gmax[g]);
             }
-            a.out[(size_t)(h * G + g) * HD + d] = __fmul_rn(s, __fdiv_rn(1.0f, l));
+        } else {
+            for (uint32_t i = o0 + warp; i < o1; i += NW) {
+                const uint32_t g = i / HD, d = i % HD;
+                const size_t row = (size_t)(h * G + g) * a.n_chunks;
+                float s = 0.0f;
+                for (uint32_t k = lane; k < n_act; k += 32) s += __ldcg(&a.opart[(row + k) * HD + d]);
+                s = warp_sum(s);
+                if (lane == 0) a.out[(size_t)(h * G + g) * HD + d] = __fmul_rn(s, gmax[g]);
+            }
         }
     }
     // last CTA of the head resets the counters for the next launch

@@ -7,21 +7,34 @@
 // (silu.c:18-94 + mul_fp32.c:17-127) and the residual add (add_fp32.c:17-165)
 // run as epilogues.
 //
-// Device weight layout ("stream tiles"): rows are grouped R at a time; a
-// tile is the R rows' 16-byte nibble planes ([R][nb][16], the upstream qs
-// bytes unchanged) followed by their fp32 scales ([R][nb]), nb = K/32.
-// Tiles are contiguous in HBM, so a tile is one 1-D bulk copy.
+// Arithmetic.  A Q4_0 block contributes s * sum_k (q_k - 8) x_k.  The kernel
+// evaluates sum_k q_k x_k EXACTLY on the integer tensor cores: the block's 32
+// inputs are put on a common fixed-point grid (X_k = rint(x_k * 2^(22-e)),
+// e the exponent of the block max, |X_k| < 2^22) and split into three signed
+// int8 limbs (X = a*65536 + b*256 + c); one mma.sync m16n8k32 u8 x s8 -> s32
+// multiplies 16 weight rows (q as u8, no float conversion at all) by the
+// three limb columns with exact int32 sums.  The limbs are recombined and
+// the -8*sum(X) term added in fp32, then scaled by s * 2^-(22-e).  The only
+// approximations are the 2^-23 (relative to the block max) input grid and
+// fp32 accumulation across blocks — the error of an fp32 dot product.
+// Versus dequantising to fp32 this needs ~1.4 instead of ~4 instructions
+// per weight, so the kernel is HBM-bound rather than issue-bound.
 //
-// CTA = (nb/BPT)*c consumer threads + 1 producer warp.  Consumer thread t
-// owns the BPT block columns cb, cb+nb/BPT, ... (cb = t % (nb/BPT)) of every
-// row r with r % c == t / (nb/BPT); its 32*BPT inputs live in registers for
-// the whole kernel.  The producer warp streams this CTA's tiles through an
-// NSTAGE shared-memory ring with cp.async.bulk + mbarrier (transaction
-// bytes); weight loads do not depend on the previous kernel, so they start
-// before the programmatic-dependent-launch wait.  Dequantisation builds
-// 2^23+q floats with one PRMT per nibble, subtracts 2^23+8 exactly (packed
-// FADD2) and accumulates with packed FFMA2; per row the block partials
-// s_b*dot_b are summed by one warp from shared memory.
+// Device weight layout ("slab tiles"): rows in slabs of 16; for each
+// (slab, block) 320 bytes: 256 bytes of mma A fragments (lane-major, 8 bytes
+// per lane: low nibbles = k 4t..4t+3, high nibbles = k 16+4t..16+4t+3 for
+// rows g and g+8, g = lane/4, t = lane%4) then 16 fp32 scales laid out
+// [g][row g, row g+8].  Blocks of a slab are contiguous, slabs follow each
+// other, so any range of blocks is one 1-D bulk copy.
+//
+// Work split.  The grid's CTAs take equal contiguous ranges of the block
+// sequence (slab-major), so every CTA streams the same bytes.  A slab cut
+// by a range boundary is finished by the last of its CTAs to arrive
+// (per-slab ticket in global scratch), which adds the parts in CTA order.
+// Inside a CTA a producer warp streams stages through a shared-memory ring
+// with cp.async.bulk + mbarrier; weight loads start before the programmatic
+// dependent launch wait.  Consumer warp w handles the blocks of a slab with
+// index = w (mod 8), so all sums run in a fixed order (deterministic).
 #pragma once
 
 #include "common.cuh"
@@ -42,11 +55,18 @@ struct StepParams {  // device-resident per-step scalars (graph-replay friendly)
     uint32_t valid;  // positions 0..valid-1 are unmasked for this row
 };
 
+static constexpr int GEMV_CONSUMER_WARPS = 8;
+static constexpr int GEMV_THREADS = GEMV_CONSUMER_WARPS * 32 + 32;
+static constexpr uint32_t GEMV_BLOCK_BYTES = 320;  // one (slab, block) unit
+static constexpr uint32_t GEMV_BFRAG_BYTES = 96;   // x limb fragments of a block (12 lanes)
+
 struct GemvArgs {
-    const uint8_t* w;          // packed stream tiles
-    uint32_t M, K, R, c;       // rows, cols, rows per tile, row groups per tile
-    uint32_t bpt;              // Q4 blocks per consumer thread per row (template)
-    uint32_t n_tiles;
+    const uint8_t* w;          // packed slab tiles
+    uint32_t M, K;             // rows, cols
+    uint32_t n_slabs, nb;      // slabs of 16 rows, blocks per row
+    uint32_t stage_blocks;     // blocks per ring stage
+    uint32_t n_stage;          // ring depth
+    uint32_t max_parts;        // CTAs that can share one slab
     const float* x;            // input vector, or the embedding table if gather
     const StepParams* step;    // per-step scalars (token, pos)
     uint32_t gather;           // non-zero: x row = x + step->token * K (embedding)
@@ -56,6 +76,8 @@ struct GemvArgs {
     float* y;
     const float* resid;
     int epi;
+    float* part;               // scratch [n_slabs][max_parts][16]
+    uint32_t* ticket;          // scratch [n_slabs], zero between launches
     // EPI_QKV
     const float* rope_cos;     // [max_seq][hd] duplicated-pair tables
     const float* rope_sin;
@@ -63,18 +85,23 @@ struct GemvArgs {
     uint32_t hd, q_rows, kv_rows, max_seq;
 };
 
-static constexpr int GEMV_NSTAGE = 4;
-static constexpr int GEMV_MAX_CONSUMERS = 256;
-
-__host__ __device__ inline uint32_t gemv_tile_bytes(uint32_t R, uint32_t K) {
-    return R * (K / 32) * 20u;
+// Shared memory: ring | bfrag[nb][96] | fsc[nb] float2 | red[2][8][16] | bars | misc
+__host__ __device__ inline size_t gemv_smem_bytes(uint32_t nb, uint32_t stage_blocks,
+                                                  uint32_t n_stage) {
+    return (size_t)n_stage * stage_blocks * GEMV_BLOCK_BYTES + (size_t)nb * GEMV_BFRAG_BYTES +
+           (size_t)nb * 8 + 2 * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 + 64 * 4 + 128;
 }
 
-// Shared memory: ring | red[2][R*nb/BPT] | barriers | rms partials
-__host__ __device__ inline size_t gemv_smem_bytes(uint32_t R, uint32_t K, uint32_t bpt) {
-    size_t tile = gemv_tile_bytes(R, K);
-    size_t red = 2ull * R * (K / 32 / bpt) * 4;
-    return GEMV_NSTAGE * tile + red + 2 * GEMV_NSTAGE * 8 + 64 * 4 + 64;
+__host__ __device__ inline uint32_t range_begin(uint64_t n, uint32_t i, uint32_t G) {
+    return (uint32_t)(n * i / G);
+}
+
+// Largest CTA index whose range starts at or before block x.
+__device__ __forceinline__ uint32_t cta_of(uint64_t n, uint32_t G, uint64_t x) {
+    uint32_t i = (uint32_t)(x * G / n);
+    while (i + 1 < G && range_begin(n, i + 1, G) <= x) ++i;
+    while (i > 0 && range_begin(n, i, G) > x) --i;
+    return i;
 }
 
 __device__ __forceinline__ void rope_pair(float v0, float v1, const float* ct,
@@ -85,31 +112,77 @@ __device__ __forceinline__ void rope_pair(float v0, float v1, const float* ct,
     o1 = __fadd_rn(__fmul_rn(v1, ct[e + 1]), __fmul_rn(v0, st[e + 1]));
 }
 
-// BPT: Q4 blocks per thread per row; ROWS: rows per thread per tile (R / c).
-template <int BPT, int ROWS>
-__global__ void __launch_bounds__(GEMV_MAX_CONSUMERS + 32, 2) gemv_q4_kernel(const GemvArgs a) {
+__device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Epilogue for lanes 0..15 of one warp holding the 16 finished rows of slab j
+// (lane = row within the slab).  Pairs use the odd lane's value via shuffle.
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uint32_t lane, float v) {
+    const float vn = __shfl_down_sync(0x0000ffffu, v, 1, 16);
+    const uint32_t row = j * 16 + lane;
+    if (row >= a.M) return;
+    if (a.epi == EPI_STORE) {
+        a.y[row] = v;
+    } else if (a.epi == EPI_RESID) {
+        a.y[row] = __fadd_rn(a.resid[row], v);
+    } else if (lane & 1) {
+        return;  // pairs: the even lane writes both
+    } else if (a.epi == EPI_SILU) {
+        // upstream silu.c (poly exp on the vector body) then mul_fp32.c
+        a.y[row / 2] = __fmul_rn(silu_poly(v), vn);
+    } else {  // EPI_QKV
+        const uint32_t pos = a.step->pos;
+        const float* ct = a.rope_cos + (size_t)pos * a.hd;
+        const float* st = a.rope_sin + (size_t)pos * a.hd;
+        float o0, o1;
+        if (row < a.q_rows) {
+            rope_pair(v, vn, ct, st, row % a.hd, o0, o1);
+            a.y[row] = o0;
+            a.y[row + 1] = o1;
+        } else if (row < a.q_rows + a.kv_rows) {
+            const uint32_t kr = row - a.q_rows, h = kr / a.hd, e = kr % a.hd;
+            rope_pair(v, vn, ct, st, e, o0, o1);
+            float* dst = a.kv_layer + ((size_t)h * a.max_seq + pos) * 2 * a.hd + e;
+            dst[0] = o0;
+            dst[1] = o1;
+        } else {
+            const uint32_t vr = row - a.q_rows - a.kv_rows, h = vr / a.hd, e = vr % a.hd;
+            float* dst = a.kv_layer + ((size_t)h * a.max_seq + pos) * 2 * a.hd + a.hd + e;
+            dst[0] = v;
+            dst[1] = vn;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t nb = a.K / 32;
-    const uint32_t nbc = nb / BPT;       // block columns per row group
-    const uint32_t T = nbc * a.c;        // consumer threads
-    const uint32_t tile_bytes = gemv_tile_bytes(a.R, a.K);
+    constexpr uint32_t NW = GEMV_CONSUMER_WARPS, T = NW * 32;
+    const uint32_t nb = a.nb;
+    const uint32_t stage_bytes = a.stage_blocks * GEMV_BLOCK_BYTES;
     uint8_t* ring = smem;
-    float* red = reinterpret_cast<float*>(smem + GEMV_NSTAGE * tile_bytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * a.R * nbc);
-    uint64_t* empty = full + GEMV_NSTAGE;
-    float* rms_part = reinterpret_cast<float*>(empty + GEMV_NSTAGE);
+    uint8_t* bfrag = ring + (size_t)a.n_stage * stage_bytes;
+    float2* fsc = reinterpret_cast<float2*>(bfrag + (size_t)nb * GEMV_BFRAG_BYTES);
+    float* red = reinterpret_cast<float*>(fsc + nb);             // [2][NW][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * NW * 16);
+    uint64_t* empty = full + 8;
+    float* rms_part = reinterpret_cast<float*>(empty + 8);
 
     const uint32_t tid = threadIdx.x;
-    const uint32_t G = gridDim.x;
-    const uint32_t t0 = (uint32_t)((uint64_t)a.n_tiles * blockIdx.x / G);
-    const uint32_t t1 = (uint32_t)((uint64_t)a.n_tiles * (blockIdx.x + 1) / G);
-    const uint32_t n_my = t1 - t0;
-    const uint32_t n_cwarps = T / 32;
+    const uint32_t G = gridDim.x, cta = blockIdx.x;
+    const uint64_t NB = (uint64_t)a.n_slabs * nb;
+    const uint32_t x0 = range_begin(NB, cta, G), x1 = range_begin(NB, cta + 1, G);
+    const uint32_t n_stages = (x1 - x0 + a.stage_blocks - 1) / a.stage_blocks;
 
     if (tid == 0) {
-        for (int s = 0; s < GEMV_NSTAGE; ++s) {
+        for (uint32_t s = 0; s < a.n_stage; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], n_cwarps);
+            mbar_init(&empty[s], NW);
         }
         fence_mbar_init();
     }
@@ -117,30 +190,30 @@ __global__ void __launch_bounds__(GEMV_MAX_CONSUMERS + 32, 2) gemv_q4_kernel(con
     pdl_trigger();
 
     if (tid >= T) {
-        // ---- producer warp: stream this CTA's tiles ----------------------
+        // ---- producer warp: stream this CTA's block range -------------------
         if (tid == T) {
             const uint64_t pol = l2_evict_first_policy();
-            for (uint32_t k = 0; k < n_my; ++k) {
-                const uint32_t s = k % GEMV_NSTAGE;
-                if (k >= GEMV_NSTAGE &&
-                    !mbar_wait(&empty[s], ((k / GEMV_NSTAGE) & 1) ^ 1, QDEV_WAIT_EMPTY_TIMEOUT))
+            for (uint32_t k = 0; k < n_stages; ++k) {
+                const uint32_t s = k % a.n_stage;
+                if (k >= a.n_stage &&
+                    !mbar_wait(&empty[s], ((k / a.n_stage) & 1) ^ 1, QDEV_WAIT_EMPTY_TIMEOUT))
                     break;
-                mbar_arrive_expect_tx(&full[s], tile_bytes);
-                bulk_g2s(ring + (size_t)s * tile_bytes,
-                         a.w + (size_t)(t0 + k) * tile_bytes, tile_bytes, &full[s], pol);
+                const uint32_t b0 = x0 + k * a.stage_blocks;
+                const uint32_t n = min(a.stage_blocks, x1 - b0);
+                mbar_arrive_expect_tx(&full[s], n * GEMV_BLOCK_BYTES);
+                bulk_g2s(ring + (size_t)s * stage_bytes, a.w + (size_t)b0 * GEMV_BLOCK_BYTES,
+                         n * GEMV_BLOCK_BYTES, &full[s], pol);
             }
         }
         pdl_wait();  // every thread waits: the grid ends after its predecessor
         return;
     }
 
-    // ---- consumers -----------------------------------------------------------
+    // ---- consumers: input prologue -------------------------------------------
     pdl_wait();
-    const uint32_t cb = tid % nbc, g = tid / nbc;
     const uint32_t lane = tid & 31, warp = tid >> 5;
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)a.step->token * a.K;
-
     float r_norm = 1.0f;
     if (a.norm_w) {
         // upstream rmsnorm.c: mean of squares, rsqrt + one Newton step
@@ -150,155 +223,173 @@ __global__ void __launch_bounds__(GEMV_MAX_CONSUMERS + 32, 2) gemv_q4_kernel(con
         if (lane == 0) rms_part[warp] = ss;
         asm volatile("bar.sync 1, %0;" ::"r"(T));
         float tot = 0.0f;
-        for (uint32_t i = 0; i < n_cwarps; ++i) tot += rms_part[i];
+        for (uint32_t i = 0; i < NW; ++i) tot += rms_part[i];
         float me = __fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps);
         float r0 = __fdiv_rn(1.0f, __fsqrt_rn(me));
         float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0, r0)));
         r_norm = __fmul_rn(__fmul_rn(r0, tm), 0.5f);
     }
-    if (a.x_copy && blockIdx.x == 0)
+    if (a.x_copy && cta == 0)
         for (uint32_t i = tid; i < a.K; i += T) a.x_copy[i] = xs[i];
-
-    float2 xr[BPT][16];
+    // Fixed-point limbs of every input block: warp w handles blocks w, w+8, ...
+    // lane j holds element 32b + j.  B fragment of lane L = g*4 + t (g < 3 =
+    // limb): word 0 = limb g of k 4t..4t+3, word 1 = limb g of k 16+4t..16+4t+3.
+    for (uint32_t b = warp; b < nb; b += NW) {
+        float xv = xs[(size_t)b * 32 + lane];
+        if (a.norm_w) xv = __fmul_rn(__fmul_rn(xv, r_norm), a.norm_w[(size_t)b * 32 + lane]);
+        const float m = warp_max(fabsf(xv));
+        int e = 0;
+        if (m > 0.0f) frexpf(m, &e);
+        const int sh = 22 - e;
+        const int X = __float2int_rn(ldexpf(xv, sh));  // |X| < 2^22
+        const int c8 = (int)(int8_t)(X & 0xFF);
+        const int X1 = (X - c8) >> 8;
+        const int b8 = (int)(int8_t)(X1 & 0xFF);
+        const int a8 = (X1 - b8) >> 8;
+        int sx = X;
 #pragma unroll
-    for (int bi = 0; bi < BPT; ++bi) {
-        const uint32_t b = cb + bi * nbc;
-        const float4* x4 = reinterpret_cast<const float4*>(xs + (size_t)b * 32);
-        const float4* g4 = a.norm_w ? reinterpret_cast<const float4*>(a.norm_w + (size_t)b * 32)
-                                    : nullptr;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            float4 v = x4[i];
-            if (g4) {
-                float4 gw = g4[i];
-                v.x = __fmul_rn(__fmul_rn(v.x, r_norm), gw.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, r_norm), gw.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, r_norm), gw.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, r_norm), gw.w);
-            }
-            xr[bi][2 * i] = make_float2(v.x, v.y);
-            xr[bi][2 * i + 1] = make_float2(v.z, v.w);
+        for (int o = 16; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+        uint8_t* bf = bfrag + (size_t)b * GEMV_BFRAG_BYTES;
+        const uint32_t t = (lane & 15) >> 2, wd = lane >> 4, by = lane & 3;
+        const uint32_t off = t * 8 + wd * 4 + by;
+        bf[0 * 32 + off] = (uint8_t)a8;
+        bf[1 * 32 + off] = (uint8_t)b8;
+        bf[2 * 32 + off] = (uint8_t)c8;
+        if (lane == 0) {
+            const float f = ldexpf(1.0f, -sh);
+            fsc[b] = make_float2(f, f * (-8.0f * (float)sx));
         }
     }
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
 
-    const bool pairs = (a.epi == EPI_QKV || a.epi == EPI_SILU);
-    const uint32_t units = pairs ? a.R / 2 : a.R;
-
-    // Dequantisation: one PRMT moves a nibble (pre-masked into the low half
-    // of a byte) under the exponent byte 0x4B, giving the float 2^23 + q; a
-    // packed subtract of 2^23 + 8 then yields q - 8 exactly.  (Folding the
-    // -8 into a block-sum correction instead saves that subtract but costs
-    // ~4 bits through cancellation, which long-context attention amplified
-    // past the parity tolerance.)
-    const float2 bias = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
-    for (uint32_t k = 0; k < n_my; ++k) {
-        const uint32_t s = k % GEMV_NSTAGE;
-        const bool ok = mbar_wait(&full[s], (k / GEMV_NSTAGE) & 1, QDEV_WAIT_FULL_TIMEOUT);
-        const uint8_t* tile = ring + (size_t)s * tile_bytes;
-        const uint4* qs = reinterpret_cast<const uint4*>(tile);
-        const float* sc = reinterpret_cast<const float*>(tile + (size_t)a.R * nb * 16);
-        float* rb = red + (k & 1) * a.R * nbc;
-#pragma unroll
-        for (int j = 0; j < ROWS; ++j) {
-            const uint32_t r = g + a.c * j;
-            float part = 0.0f;
-#pragma unroll
-            for (int bi = 0; bi < BPT; ++bi) {
-                const uint32_t b = cb + bi * nbc;
-                const uint4 q = qs[r * nb + b];
-                const float scale = sc[r * nb + b];
-                float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-                const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int wi = 0; wi < 4; ++wi) {
-                    const uint32_t lo = words[wi] & 0x0F0F0F0Fu;
-                    const uint32_t hi = (words[wi] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-                    for (int m = 0; m < 4; ++m) {
-                        const uint32_t sel = 0x7540u | (uint32_t)m;
-                        float2 d = make_float2(__uint_as_float(prmt(lo, 0x4B000000u, sel)),
-                                               __uint_as_float(prmt(hi, 0x4B000000u, sel)));
-                        d = __fadd2_rn(d, bias);  // exactly q - 8
-                        if (m & 1) acc1 = __ffma2_rn(d, xr[bi][4 * wi + m], acc1);
-                        else acc0 = __ffma2_rn(d, xr[bi][4 * wi + m], acc0);
-                    }
-                }
-                const float dot =
-                    __fadd_rn(__fadd_rn(acc0.x, acc0.y), __fadd_rn(acc1.x, acc1.y));
-                part = __fmaf_rn(scale, dot, part);
+    // ---- main loop ---------------------------------------------------------------
+    const uint32_t g = lane >> 2, t = lane & 3;
+    // limb weights: lane t=0 holds columns (a, b) -> a*256 + b, scaled by 256;
+    // t=1 holds (c, 0) plus the -8*sum(X) correction; t=2,3 hold zeros.
+    const int m0 = t == 0 ? 256 : (t == 1 ? 1 : 0);
+    const int m1 = t == 0 ? 1 : 0;
+    const float wt = t == 0 ? 256.0f : (t == 1 ? 1.0f : 0.0f);
+    const bool has_corr = t == 1;
+    const uint32_t zero_lane = lane >= 12;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    uint32_t rbuf = 0;
+    for (uint32_t k = 0; k < n_stages; ++k) {
+        const uint32_t s = k % a.n_stage;
+        const bool ok = mbar_wait(&full[s], (k / a.n_stage) & 1, QDEV_WAIT_FULL_TIMEOUT);
+        const uint8_t* stage = ring + (size_t)s * stage_bytes;
+        const uint32_t sb0 = x0 + k * a.stage_blocks;
+        const uint32_t sb1 = min(sb0 + a.stage_blocks, x1);
+        for (uint32_t seg = sb0; seg < sb1;) {
+            const uint32_t j = seg / nb, jb = j * nb;
+            const uint32_t seg_end = min(sb1, jb + nb);
+            // this warp's blocks of the segment: (b - jb) % NW == warp
+            uint32_t b = seg + ((warp + NW - (seg - jb) % NW) % NW);
+            for (; b < seg_end; b += NW) {
+                const uint8_t* blk = stage + (size_t)(b - sb0) * GEMV_BLOCK_BYTES;
+                const uint2 q = *reinterpret_cast<const uint2*>(blk + lane * 8);
+                const uint32_t kb = b - jb;
+                uint2 bv = make_uint2(0u, 0u);
+                if (!zero_lane) bv = *reinterpret_cast<const uint2*>(bfrag + (size_t)kb * GEMV_BFRAG_BYTES + lane * 8);
+                int d[4];
+                mma_u8s8(d, q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, (q.x >> 4) & 0x0F0F0F0Fu,
+                         (q.y >> 4) & 0x0F0F0F0Fu, bv.x, bv.y);
+                const float2 sc = *reinterpret_cast<const float2*>(blk + 256 + g * 8);
+                const float2 fz = fsc[kb];
+                const float fw = fz.x * wt;
+                const float fc = has_corr ? fz.y : 0.0f;
+                const float p0 = (float)(d[0] * m0 + d[1] * m1);
+                const float p1 = (float)(d[2] * m0 + d[3] * m1);
+                acc0 = __fmaf_rn(sc.x, __fmaf_rn(p0, fw, fc), acc0);
+                acc1 = __fmaf_rn(sc.y, __fmaf_rn(p1, fw, fc), acc1);
             }
-            rb[r * nbc + cb] = ok ? part : 0.0f;
+            if (seg_end == jb + nb || seg_end == x1) {
+                // flush slab j: limbs (quad) -> warps (smem) -> CTA parts (global)
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+                float* rb = red + rbuf * NW * 16;
+                if (t == 0) {
+                    rb[warp * 16 + g] = ok ? acc0 : 0.0f;
+                    rb[warp * 16 + g + 8] = ok ? acc1 : 0.0f;
+                }
+                acc0 = acc1 = 0.0f;
+                asm volatile("bar.sync 1, %0;" ::"r"(T));
+                if (warp == 0) {
+                    float v = 0.0f;
+                    if (lane < 16)
+#pragma unroll
+                        for (uint32_t w = 0; w < NW; ++w) v += rb[w * 16 + lane];
+                    const uint32_t c_first = cta_of(NB, G, jb);
+                    const uint32_t c_last = cta_of(NB, G, jb + nb - 1);
+                    bool finish = c_first == c_last;
+                    if (!finish) {
+                        float* pp = a.part + ((size_t)j * a.max_parts) * 16;
+                        if (lane < 16) pp[(cta - c_first) * 16 + lane] = v;
+                        __threadfence();
+                        uint32_t last = 0;
+                        if (lane == 0)
+                            last = atomicAdd(&a.ticket[j], 1u) == c_last - c_first ? 1u : 0u;
+                        last = __shfl_sync(0xffffffffu, last, 0);
+                        if (last) {
+                            __threadfence();
+                            v = 0.0f;
+                            if (lane < 16)
+                                for (uint32_t p = 0; p <= c_last - c_first; ++p)
+                                    v += __ldcg(&pp[p * 16 + lane]);
+                            if (lane == 0) a.ticket[j] = 0u;
+                            finish = true;
+                        }
+                    }
+                    if (finish && lane < 16) gemv_epilogue(a, j, lane, v);
+                }
+                rbuf ^= 1;
+            }
+            seg = seg_end;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        asm volatile("bar.sync 1, %0;" ::"r"(T));
-
-        // ---- per-row reduction + epilogue (one warp per row / row pair) ----
-        const uint32_t tile_row0 = (t0 + k) * a.R;
-        for (uint32_t u = warp; u < units; u += n_cwarps) {
-            const uint32_t r0 = pairs ? 2 * u : u;
-            float v0 = 0.0f, v1 = 0.0f;
-            for (uint32_t i = lane; i < nbc; i += 32) {
-                v0 += rb[r0 * nbc + i];
-                if (pairs) v1 += rb[(r0 + 1) * nbc + i];
-            }
-            v0 = warp_sum(v0);
-            if (pairs) v1 = warp_sum(v1);
-            if (lane != 0) continue;
-            const uint32_t row = tile_row0 + r0;
-            if (row >= a.M) continue;
-            if (a.epi == EPI_STORE) {
-                a.y[row] = v0;
-            } else if (a.epi == EPI_RESID) {
-                a.y[row] = __fadd_rn(a.resid[row], v0);
-            } else if (a.epi == EPI_SILU) {
-                // upstream silu.c (poly exp on the vector body) then mul_fp32.c
-                a.y[row / 2] = __fmul_rn(silu_poly(v0), v1);
-            } else {  // EPI_QKV
-                const uint32_t pos = a.step->pos;
-                const float* ct = a.rope_cos + (size_t)pos * a.hd;
-                const float* st = a.rope_sin + (size_t)pos * a.hd;
-                float o0, o1;
-                if (row < a.q_rows) {
-                    rope_pair(v0, v1, ct, st, row % a.hd, o0, o1);
-                    a.y[row] = o0;
-                    a.y[row + 1] = o1;
-                } else if (row < a.q_rows + a.kv_rows) {
-                    const uint32_t kr = row - a.q_rows, h = kr / a.hd, e = kr % a.hd;
-                    rope_pair(v0, v1, ct, st, e, o0, o1);
-                    float* dst = a.kv_layer + ((size_t)h * a.max_seq + pos) * 2 * a.hd + e;
-                    dst[0] = o0;
-                    dst[1] = o1;
-                } else {
-                    const uint32_t vr = row - a.q_rows - a.kv_rows, h = vr / a.hd, e = vr % a.hd;
-                    float* dst =
-                        a.kv_layer + ((size_t)h * a.max_seq + pos) * 2 * a.hd + a.hd + e;
-                    dst[0] = v0;
-                    dst[1] = v1;
-                }
-            }
-        }
     }
 }
 
-// Repack upstream AoS Q4_0 blocks ([M][nb] x 20 B) into stream tiles.
+// Repack upstream AoS Q4_0 blocks ([M][nb] x 20 B) into slab tiles.
 // interleave_half != 0: destination row 2i takes source row i and 2i+1 takes
-// source row interleave_half + i (gate/up pairing).
+// source row interleave_half + i (gate/up pairing).  Rows >= M are zero.
 __global__ void q4_pack_kernel(const uint8_t* __restrict__ src, uint32_t M, uint32_t K,
-                               uint32_t R, uint32_t interleave_half, uint8_t* __restrict__ dst) {
+                               uint32_t interleave_half, uint8_t* __restrict__ dst) {
     const uint32_t nb = K / 32;
-    const uint64_t n = (uint64_t)M * nb;
+    const uint32_t n_slabs = (M + 15) / 16;
+    const uint64_t n = (uint64_t)n_slabs * nb * 32;  // one thread per (slab, block, lane)
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint32_t drow = (uint32_t)(i / nb), b = (uint32_t)(i % nb);
-        uint32_t srow = drow;
-        if (interleave_half) srow = (drow & 1) ? interleave_half + drow / 2 : drow / 2;
-        const uint32_t* s = reinterpret_cast<const uint32_t*>(src + ((size_t)srow * nb + b) * 20);
-        const uint32_t tile = drow / R, r = drow % R;
-        uint8_t* tb = dst + (size_t)tile * gemv_tile_bytes(R, K);
-        uint4 q = make_uint4(s[0], s[1], s[2], s[3]);
-        *reinterpret_cast<uint4*>(tb + ((size_t)r * nb + b) * 16) = q;
-        *reinterpret_cast<uint32_t*>(tb + (size_t)R * nb * 16 + ((size_t)r * nb + b) * 4) = s[4];
+        const uint32_t lane = (uint32_t)(i % 32);
+        const uint64_t sb = i / 32;
+        const uint32_t b = (uint32_t)(sb % nb), j = (uint32_t)(sb / nb);
+        const uint32_t g = lane >> 2, t = lane & 3;
+        uint8_t* out = dst + sb * GEMV_BLOCK_BYTES;
+        uint32_t words[2];
+        float scales[2];
+        for (int half = 0; half < 2; ++half) {
+            const uint32_t drow = j * 16 + g + 8 * half;
+            uint32_t wv = 0;
+            float sv = 0.0f;
+            if (drow < M) {
+                uint32_t srow = drow;
+                if (interleave_half) srow = (drow & 1) ? interleave_half + drow / 2 : drow / 2;
+                const uint8_t* blk = src + ((size_t)srow * nb + b) * 20;
+                for (int by = 0; by < 4; ++by) {
+                    const uint32_t klo = 4 * t + by, khi = 16 + 4 * t + by;
+                    const uint32_t nlo = (blk[klo / 2] >> ((klo & 1) * 4)) & 15;
+                    const uint32_t nhi = (blk[khi / 2] >> ((khi & 1) * 4)) & 15;
+                    wv |= (nlo | (nhi << 4)) << (8 * by);
+                }
+                memcpy(&sv, blk + 16, 4);
+            }
+            words[half] = wv;
+            scales[half] = sv;
+        }
+        *reinterpret_cast<uint2*>(out + lane * 8) = make_uint2(words[0], words[1]);
+        if (t == 0) *reinterpret_cast<float2*>(out + 256 + g * 8) = make_float2(scales[0], scales[1]);
     }
 }
 

@@ -37,9 +37,18 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     if (!(s->hd == 32 || s->hd == 64 || s->hd == 128) || G > (uint32_t)ATT_MAXG ||
         c.n_heads % c.n_kv_heads || c.max_seq_len == 0)
         return Q_ERR_INVALID_CONFIG;
-    if (!plan_gemv(D + 2 * s->kvd, D, true, s->p_qkv) || !plan_gemv(D, D, false, s->p_wo) ||
-        !plan_gemv(2 * H, D, true, s->p_gu) || !plan_gemv(D, H, false, s->p_down))
+    if (!plan_gemv(D + 2 * s->kvd, D, s->p_qkv) || !plan_gemv(D, D, s->p_wo) ||
+        !plan_gemv(2 * H, D, s->p_gu) || !plan_gemv(D, H, s->p_down))
         return Q_ERR_INVALID_CONFIG;
+    {
+        const size_t sb = std::max(std::max(s->p_qkv.scratch_bytes(), s->p_wo.scratch_bytes()),
+                                   std::max(s->p_gu.scratch_bytes(), s->p_down.scratch_bytes()));
+        void* sp = nullptr;
+        q_error_code r = dalloc(s, &sp, sb);
+        if (r != Q_OK) return r;
+        if (!cuda_ok(cudaMemset(sp, 0, sb), "memset(gemv scratch)")) return Q_ERR_INVALID_ARG;
+        s->gemv_scratch = sp;
+    }
     cudaStream_t st = s->stream;
     const size_t nbD = D / 32, nbH = H / 32;
     const size_t qkv_aos = (size_t)(D + 2 * s->kvd) * nbD * 20;
@@ -252,7 +261,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         g.q_rows = D;
         g.kv_rows = s->kvd;
         g.max_seq = c.max_seq_len;
-        e = launch_gemv(s->p_qkv, g, st, l != 0);
+        e = launch_gemv(s->p_qkv, g, s->gemv_scratch, st, l != 0);
         if (e == cudaSuccess) e = enqueue_attention(s, kvl, st);
         if (e != cudaSuccess) break;
         GemvArgs o{};
@@ -262,7 +271,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         o.y = s->x;
         o.resid = s->x;
         o.epi = EPI_RESID;
-        e = launch_gemv(s->p_wo, o, st, true);
+        e = launch_gemv(s->p_wo, o, s->gemv_scratch, st, true);
         if (e != cudaSuccess) break;
         GemvArgs u{};
         u.w = s->gu[l];
@@ -272,7 +281,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         u.eps = c.rms_norm_eps;
         u.y = s->h;
         u.epi = EPI_SILU;
-        e = launch_gemv(s->p_gu, u, st, true);
+        e = launch_gemv(s->p_gu, u, s->gemv_scratch, st, true);
         if (e != cudaSuccess) break;
         GemvArgs d{};
         d.w = s->down[l];
@@ -281,7 +290,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         d.y = s->x;
         d.resid = s->x;
         d.epi = EPI_RESID;
-        e = launch_gemv(s->p_down, d, st, true);
+        e = launch_gemv(s->p_down, d, s->gemv_scratch, st, true);
     }
     return e;
 }

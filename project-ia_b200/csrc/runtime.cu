@@ -61,74 +61,84 @@ q_error_code check_device_status(const char* where) {
 // next kernel's CTA fits beside this one under programmatic dependent
 // launch).  Threads: (nb/bpt)*c <= 256, a multiple of 32.
 
-bool plan_gemv(uint32_t M, uint32_t K, bool pairs, GemvPlan& p) {
+bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     if (M == 0 || K == 0 || K % 32) return false;
-    const uint32_t nb = K / 32;
-    uint32_t R = 1;
-    while (R * 2 <= 128 && (uint64_t)R * 2 * nb * 20 <= 24576) R *= 2;
-    if (pairs && R < 2) R = 2;
-    while ((R * nb) % 4) R *= 2;  // tiles are whole 16-byte units
-    uint32_t bpt = 0, c = 0;
-    for (uint32_t b = 1; b <= 2 && !bpt; b *= 2) {
-        if (nb % b) continue;
-        const uint32_t nbc = nb / b;
-        for (uint32_t cc = R; cc >= 1; cc /= 2) {
-            const uint32_t T = nbc * cc;
-            if (T <= (uint32_t)GEMV_MAX_CONSUMERS && T % 32 == 0) {
-                bpt = b;
-                c = cc;
-                break;
-            }
-        }
+    const uint32_t nb = K / 32, n_slabs = (M + 15) / 16;
+    if (n_slabs > GemvPlan::kTicketWords) return false;
+    const uint64_t NB = (uint64_t)n_slabs * nb;
+    const int sms = device_sms();
+    const size_t fixed = gemv_smem_bytes(nb, 0, 0);
+    uint32_t stage_blocks = 64;  // 20 KB stages
+    uint32_t per_sm = 2, n_stage = 0;
+    // two CTAs per SM (the next kernel's CTA also fits under programmatic
+    // dependent launch) when a >= 2-stage ring fits in ~113 KB, else one
+    for (; per_sm >= 1; --per_sm) {
+        const size_t budget = per_sm == 2 ? 113 * 1024 : 220 * 1024;
+        if (budget <= fixed) continue;
+        n_stage = (uint32_t)std::min<size_t>(per_sm == 2 ? 4 : 8,
+                                             (budget - fixed) / (stage_blocks * GEMV_BLOCK_BYTES));
+        if (n_stage >= 2) break;
     }
-    if (!bpt) return false;
-    if (R / c > 4) R = 4 * c;  // kernels are instantiated for 1, 2 or 4 rows per thread
-    if ((R * nb) % 4) return false;
+    if (per_sm < 1 || n_stage < 2) return false;
     p.M = M;
     p.K = K;
-    p.R = R;
-    p.c = c;
-    p.bpt = bpt;
-    p.n_tiles = (M + R - 1) / R;
-    p.grid = std::min<uint32_t>(p.n_tiles, 2u * (uint32_t)device_sms());  // 2 CTAs per SM
-    p.threads = nb / bpt * c + 32;
-    p.smem = gemv_smem_bytes(R, K, bpt);
-    p.packed_bytes = (size_t)p.n_tiles * gemv_tile_bytes(R, K);
+    p.n_slabs = n_slabs;
+    p.nb = nb;
+    p.stage_blocks = stage_blocks;
+    p.n_stage = n_stage;
+    p.grid = (uint32_t)std::min<uint64_t>(NB, (uint64_t)per_sm * sms);
+    const uint64_t per_cta = std::max<uint64_t>(1, NB / p.grid);
+    p.max_parts = (uint32_t)((nb + per_cta - 1) / per_cta + 2);
+    p.smem = gemv_smem_bytes(nb, stage_blocks, n_stage);
+    p.packed_bytes = (size_t)NB * GEMV_BLOCK_BYTES;
     return true;
 }
 
-cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, cudaStream_t s, bool pdl) {
+cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, void* scratch, cudaStream_t s, bool pdl) {
     a.M = p.M;
     a.K = p.K;
-    a.R = p.R;
-    a.c = p.c;
-    a.bpt = p.bpt;
-    a.n_tiles = p.n_tiles;
-    using Kern = void (*)(GemvArgs);
-    static const Kern table[2][3] = {
-        {gemv_q4_kernel<1, 1>, gemv_q4_kernel<1, 2>, gemv_q4_kernel<1, 4>},
-        {gemv_q4_kernel<2, 1>, gemv_q4_kernel<2, 2>, gemv_q4_kernel<2, 4>}};
+    a.n_slabs = p.n_slabs;
+    a.nb = p.nb;
+    a.stage_blocks = p.stage_blocks;
+    a.n_stage = p.n_stage;
+    a.max_parts = p.max_parts;
+    a.ticket = reinterpret_cast<uint32_t*>(scratch);
+    a.part = reinterpret_cast<float*>(a.ticket + GemvPlan::kTicketWords);
     static std::once_flag once;
     std::call_once(once, [] {
-        for (auto& row : table)
-            for (Kern k : row)
-                cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(gemv_q4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     });
-    const uint32_t rows = p.R / p.c;
-    const int ri = rows == 1 ? 0 : rows == 2 ? 1 : rows == 4 ? 2 : -1;
-    if (ri < 0 || (p.bpt != 1 && p.bpt != 2)) return cudaErrorInvalidValue;
-    return launch_ex(table[p.bpt - 1][ri], dim3(p.grid), dim3(p.threads), p.smem, s, pdl, a);
+    return launch_ex(gemv_q4_kernel, dim3(p.grid), dim3(GEMV_THREADS), p.smem, s, pdl, a);
 }
 
 cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,
                     uint8_t* d_dst, cudaStream_t s) {
-    cudaError_t e = cudaMemsetAsync(d_dst, 0, p.packed_bytes, s);
-    if (e != cudaSuccess) return e;
-    const uint64_t n = (uint64_t)p.M * (p.K / 32);
+    const uint64_t n = (uint64_t)p.n_slabs * p.nb * 32;
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 65535);
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
-    q4_pack_kernel<<<blocks, 256, 0, s>>>(d_aos, p.M, p.K, p.R, interleave_half, d_dst);
+    q4_pack_kernel<<<blocks, 256, 0, s>>>(d_aos, p.M, p.K, interleave_half, d_dst);
     return cudaGetLastError();
+}
+
+void* op_gemv_scratch(const GemvPlan& p) {
+    static std::mutex mu;
+    static std::unordered_map<int, std::pair<void*, size_t>> bufs;  // device -> buffer
+    std::lock_guard<std::mutex> lk(mu);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto& b = bufs[dev];
+    if (b.second < p.scratch_bytes()) {
+        if (b.first) {
+            cudaDeviceSynchronize();
+            cudaFree(b.first);
+        }
+        b = {nullptr, 0};
+        void* q = nullptr;
+        if (!cuda_ok(cudaMalloc(&q, p.scratch_bytes()), "cudaMalloc(gemv scratch)")) return nullptr;
+        if (!cuda_ok(cudaMemset(q, 0, p.scratch_bytes()), "memset(gemv scratch)")) return nullptr;
+        b = {q, p.scratch_bytes()};
+    }
+    return b.first;
 }
 
 // ---- per-context registry ---------------------------------------------------------

@@ -35,14 +35,27 @@ cudaStream_t op_stream();  // stream for the kernel-level entry points
 // ---- GEMV launch plan ---------------------------------------------------------
 
 struct GemvPlan {
-    uint32_t M = 0, K = 0, R = 0, c = 0, bpt = 0, n_tiles = 0, grid = 0, threads = 0;
+    uint32_t M = 0, K = 0, n_slabs = 0, nb = 0, stage_blocks = 0, n_stage = 0, max_parts = 0;
+    uint32_t grid = 0;
     size_t smem = 0, packed_bytes = 0;
+    // Scratch layout, shared by every plan: a fixed ticket area of
+    // kTicketWords uint32 (zero between launches: each finisher resets its
+    // ticket), then the partial sums [n_slabs][max_parts][16] fp32.
+    static constexpr size_t kTicketWords = 16384;
+    size_t scratch_floats() const { return (size_t)n_slabs * max_parts * 16; }
+    size_t scratch_bytes() const { return kTicketWords * 4 + scratch_floats() * 4; }
 };
 
-bool plan_gemv(uint32_t M, uint32_t K, bool pairs, GemvPlan& p);
-cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, cudaStream_t s, bool pdl);
+bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p);
+// scratch: scratch_bytes() of device memory whose ticket words (the tail,
+// n_slabs uint32 after the parts) are zero before the first launch; the
+// kernel leaves them zero again.
+cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, void* scratch, cudaStream_t s, bool pdl);
 cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,
                     uint8_t* d_dst, cudaStream_t s);
+// Library-owned, zeroed GEMV scratch of the current device for the
+// kernel-level entry points (grown on demand; nullptr on failure).
+void* op_gemv_scratch(const GemvPlan& p);
 
 template <typename Kern, typename Args>
 cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
@@ -82,6 +95,7 @@ struct DevState {
     float* out_w = nullptr;
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
+    void* gemv_scratch = nullptr;  // split-slab partial sums + tickets (max over the 4 plans)
     std::vector<void*> weight_allocs;
     // activations (device arena, below the watermark)
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
