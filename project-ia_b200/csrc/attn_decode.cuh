@@ -16,13 +16,13 @@
 //
 // One kernel, grid (n_kv_heads, NC), launched cooperatively so all CTAs are
 // co-resident.  The G query heads of a KV head share its CTAs, so every K/V
-// row is read once.  At run time the valid positions are split over the
-// first n_act <= NC CTAs of each head, which then pass three phases:
-//   1. scores of the chunk (HD/16 lanes per position) -> global scratch,
-//      chunk max per query head;                      | per-head barrier
-//   2. global max, exponentials, partial P.V (float4 V loads) and partial
-//      sums -> global scratch;                        | per-head barrier
-//   3. each CTA combines a slice of the G*HD outputs: sum of partials / sum.
+// row is read once.  The valid positions are split over the first n_act <=
+// NC CTAs of each head; a CTA issues all K and V loads of its chunk (in
+// sub-chunks of 64 positions) before it needs them, keeps its scores in
+// shared memory, and passes three phases:
+//   1. scores (HD/16 lanes per position), chunk max -> global | head barrier
+//   2. global max, exponentials, partial P.V and sums -> global | head barrier
+//   3. each CTA combines a slice of the G*HD outputs.
 // Barriers are atomic counters per head with bounded spins; the last CTA of
 // a head resets that head's counters for the next launch.
 #pragma once
@@ -33,13 +33,13 @@
 namespace qb200 {
 
 static constexpr int ATT_THREADS = 256;
-static constexpr int ATT_MAXG = 8;       // query heads per KV head supported
-static constexpr int ATT_MIN_CHUNK = 32; // positions per CTA before using more CTAs
+static constexpr int ATT_MAXG = 8;        // query heads per KV head supported
+static constexpr int ATT_MIN_CHUNK = 32;  // positions per CTA before using more CTAs
+static constexpr int ATT_SUB = 64;        // positions per register-resident sub-chunk
 
 struct AttnArgs {
     const float* q;          // [n_heads][hd] rotated queries
     const float* kv_layer;   // this layer's cache base
-    float* scores;           // [n_heads][max_seq]
     float* cmax;             // [n_heads][NC]
     float* opart;            // [n_heads][NC][hd]
     float* lpart;            // [n_heads][NC]
@@ -47,8 +47,13 @@ struct AttnArgs {
     float* out;              // [n_heads][hd]
     const StepParams* step;
     uint32_t n_heads, n_kv_heads, max_seq, n_chunks;  // n_chunks = NC (grid.y)
+    uint32_t chunk_alloc;    // >= ceil(max_seq / NC): shared scores per head
     float scale;             // 1/sqrtf(hd), computed on the host like upstream
 };
+
+__host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t chunk_alloc) {
+    return (size_t)G * chunk_alloc * 4;
+}
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
     uint32_t v;
@@ -76,16 +81,21 @@ __device__ __forceinline__ void head_barrier(uint32_t* ctr, uint32_t target) {
 
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnArgs a) {
-    constexpr int LPP = HD / 16;                 // lanes per position (scores)
-    constexpr int PPW = 32 / LPP;                // positions per warp step
+    constexpr int LPP = HD / 16;                 // lanes per K row (16 floats each)
+    constexpr int PPW = 32 / LPP;                // positions per warp per K round
     constexpr int NW = ATT_THREADS / 32;
+    constexpr int SUB = NW * PPW > ATT_SUB ? NW * PPW : ATT_SUB;  // positions per sub-chunk
+    constexpr int KR = SUB / (NW * PPW);         // K rounds per sub-chunk
     constexpr int VL = HD / 4;                   // lanes per V row (float4 each)
-    constexpr int PL = ATT_THREADS / VL;         // position lanes for P.V
+    constexpr int PL = ATT_THREADS / VL;         // V rows in flight per round
+    constexpr int VR = SUB / PL;                 // V rounds per sub-chunk
+    static_assert(KR >= 1 && VR >= 1, "sub-chunk too small");
+    extern __shared__ __align__(16) float sc[];  // [G][chunk_alloc]: scores, then e
     __shared__ __align__(16) float qs[ATT_MAXG][HD];
     __shared__ float wred[NW][ATT_MAXG];
     __shared__ float gmax[ATT_MAXG];
     __shared__ __align__(16) float4 ored[PL][ATT_MAXG][VL];
-    __shared__ float lred[PL][ATT_MAXG];
+    __shared__ float lsum[ATT_MAXG];
     pdl_trigger();
     pdl_wait();
     const uint32_t h = blockIdx.x, c = blockIdx.y;
@@ -99,7 +109,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* slab = a.kv_layer + (size_t)h * a.max_seq * 2 * HD;
     uint32_t* ctr = a.sync + 4 * h;
+    const uint32_t CA = a.chunk_alloc;
 
+    // V of the first sub-chunk: in flight from the start, used in phase 2
+    const uint32_t vl = tid % VL, pl = tid / VL;
+    float4 vreg[VR];
+#pragma unroll
+    for (int r = 0; r < VR; ++r) {
+        const uint32_t p = p0 + pl + r * PL;
+        vreg[r] = p < p1 ? __ldg(reinterpret_cast<const float4*>(slab + (size_t)p * 2 * HD + HD) + vl)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     for (uint32_t i = tid; i < G * HD; i += ATT_THREADS)
         qs[i / HD][i % HD] = a.q[(size_t)(h * G) * HD + i];
     __syncthreads();
@@ -110,33 +130,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
         float mx[ATT_MAXG];
 #pragma unroll
         for (int g = 0; g < ATT_MAXG; ++g) mx[g] = -INFINITY;
-        for (uint32_t base = p0 + warp * PPW; base < p1; base += NW * PPW) {
-            const uint32_t p = base + slot;
-            const bool live = p < p1;
-            const float4* kp = reinterpret_cast<const float4*>(
-                slab + (size_t)(live ? p : p0) * 2 * HD + sub * 16);
-            float4 k4[4];
+        for (uint32_t sp0 = p0; sp0 < p1; sp0 += SUB) {
+            const uint32_t sp1 = min(sp0 + SUB, p1);
+            float4 k4[KR][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) k4[i] = __ldg(kp + i);
+            for (int r = 0; r < KR; ++r) {
+                const uint32_t p = sp0 + r * NW * PPW + warp * PPW + slot;
+                const float4* kp = reinterpret_cast<const float4*>(slab + (size_t)(p < sp1 ? p : sp0) * 2 * HD + sub * 16);
 #pragma unroll
-            for (int g = 0; g < ATT_MAXG; ++g) {
-                if (g >= (int)G) break;
-                const float4* q4 = reinterpret_cast<const float4*>(&qs[g][sub * 16]);
-                float d = 0.0f;
+                for (int i = 0; i < 4; ++i) k4[r][i] = __ldg(kp + i);
+            }
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 qv = q4[i];
-                    d = __fmaf_rn(qv.x, k4[i].x, d);
-                    d = __fmaf_rn(qv.y, k4[i].y, d);
-                    d = __fmaf_rn(qv.z, k4[i].z, d);
-                    d = __fmaf_rn(qv.w, k4[i].w, d);
-                }
+            for (int r = 0; r < KR; ++r) {
+                const uint32_t p = sp0 + r * NW * PPW + warp * PPW + slot;
+                const bool live = p < sp1;
 #pragma unroll
-                for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                const float s = __fmul_rn(d, a.scale);
-                if (live) {
-                    if (sub == 0) a.scores[(size_t)(h * G + g) * a.max_seq + p] = s;
-                    mx[g] = fmaxf(mx[g], s);
+                for (int g = 0; g < ATT_MAXG; ++g) {
+                    if (g >= (int)G) break;
+                    const float4* q4 = reinterpret_cast<const float4*>(&qs[g][sub * 16]);
+                    float d = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 qv = q4[i];
+                        d = __fmaf_rn(qv.x, k4[r][i].x, d);
+                        d = __fmaf_rn(qv.y, k4[r][i].y, d);
+                        d = __fmaf_rn(qv.z, k4[r][i].z, d);
+                        d = __fmaf_rn(qv.w, k4[r][i].w, d);
+                    }
+#pragma unroll
+                    for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                    const float s = __fmul_rn(d, a.scale);
+                    if (live) {
+                        if (sub == 0) sc[g * CA + (p - p0)] = s;
+                        mx[g] = fmaxf(mx[g], s);
+                    }
                 }
             }
         }
@@ -164,36 +191,52 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
         if (lane == 0) gmax[warp] = m;
     }
     __syncthreads();
+    const uint32_t len = p1 - p0;
+    const uint32_t nvec = N < 8 ? 0u : (N / 8) * 8;
+    for (uint32_t i = tid; i < G * len; i += ATT_THREADS) {
+        const uint32_t g = i / len, pp = i % len;
+        const float x = __fsub_rn(sc[g * CA + pp], gmax[g]);
+        sc[g * CA + pp] = (p0 + pp) < nvec ? exp_poly(x) : expf(x);
+    }
+    __syncthreads();
+    if (warp < G) {
+        float l = 0.0f;
+        for (uint32_t pp = lane; pp < len; pp += 32) l += sc[warp * CA + pp];
+        l = warp_sum(l);
+        if (lane == 0) lsum[warp] = l;
+    }
     {
-        const uint32_t nvec = N < 8 ? 0u : (N / 8) * 8;
-        const uint32_t vl = tid % VL, pl = tid / VL;
         float4 o[ATT_MAXG];
-        float l[ATT_MAXG];
 #pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g) {
-            o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-            l[g] = 0.0f;
-        }
-        for (uint32_t p = p0 + pl; p < p1; p += PL) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(slab + (size_t)p * 2 * HD + HD) + vl);
+        for (int g = 0; g < ATT_MAXG; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t sp0 = p0; sp0 < p1; sp0 += SUB) {
+            if (sp0 != p0) {  // later sub-chunks (long contexts): load now
 #pragma unroll
-            for (int g = 0; g < ATT_MAXG; ++g) {
-                if (g >= (int)G) break;
-                const float x = __fsub_rn(__ldcg(&a.scores[(size_t)(h * G + g) * a.max_seq + p]), gmax[g]);
-                const float e = p < nvec ? exp_poly(x) : expf(x);
-                l[g] += e;
-                o[g].x = __fmaf_rn(e, v.x, o[g].x);
-                o[g].y = __fmaf_rn(e, v.y, o[g].y);
-                o[g].z = __fmaf_rn(e, v.z, o[g].z);
-                o[g].w = __fmaf_rn(e, v.w, o[g].w);
+                for (int r = 0; r < VR; ++r) {
+                    const uint32_t p = sp0 + pl + r * PL;
+                    vreg[r] = p < p1 ? __ldg(reinterpret_cast<const float4*>(slab + (size_t)p * 2 * HD + HD) + vl)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < VR; ++r) {
+                const uint32_t p = sp0 + pl + r * PL;
+                if (p >= p1) break;
+                const float4 v = vreg[r];
+#pragma unroll
+                for (int g = 0; g < ATT_MAXG; ++g) {
+                    if (g >= (int)G) break;
+                    const float e = sc[g * CA + (p - p0)];
+                    o[g].x = __fmaf_rn(e, v.x, o[g].x);
+                    o[g].y = __fmaf_rn(e, v.y, o[g].y);
+                    o[g].z = __fmaf_rn(e, v.z, o[g].z);
+                    o[g].w = __fmaf_rn(e, v.w, o[g].w);
+                }
             }
         }
 #pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g) {
-            if (g >= (int)G) break;
-            ored[pl][g][vl] = o[g];
-            if (vl == 0) lred[pl][g] = l[g];
-        }
+        for (int g = 0; g < ATT_MAXG; ++g)
+            if (g < (int)G) ored[pl][g][vl] = o[g];
         __syncthreads();
         for (uint32_t i = tid; i < G * VL; i += ATT_THREADS) {
             const uint32_t g = i / VL, j = i % VL;
@@ -204,18 +247,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
             }
             reinterpret_cast<float4*>(a.opart + ((size_t)(h * G + g) * a.n_chunks + c) * HD)[j] = s;
         }
-        if (tid < G) {
-            float s = 0.0f;
-            for (int q = 0; q < PL; ++q) s += lred[q][tid];
-            a.lpart[(size_t)(h * G + tid) * a.n_chunks + c] = s;
-        }
+        if (tid < G) a.lpart[(size_t)(h * G + tid) * a.n_chunks + c] = lsum[tid];
     }
     head_barrier(ctr + 1, n_act);
 
     // ---- phase 3: this CTA's slice of the outputs --------------------------------
-    // The partials sit in L2; the chunk sums are spread over lanes so every
-    // load of a warp is in flight at once (a serial loop over chunks is a
-    // chain of L2 round trips).
+    // The partials sit in L2; chunk sums are spread over lanes so every load
+    // of a warp is in flight at once.
     {
         if (warp < G) {  // softmax denominators
             float l = 0.0f;

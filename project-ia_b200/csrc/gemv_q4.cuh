@@ -92,13 +92,15 @@ __host__ __device__ inline size_t gemv_smem_bytes(uint32_t nb, uint32_t stage_bl
            (size_t)nb * 8 + 2 * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 + 64 * 4 + 128;
 }
 
-__host__ __device__ inline uint32_t range_begin(uint64_t n, uint32_t i, uint32_t G) {
-    return (uint32_t)(n * i / G);
+// CTA i owns blocks [n*i/G, n*(i+1)/G) of the slab-major block sequence
+// (host guarantees n * G < 2^32, so 32-bit arithmetic is exact).
+__host__ __device__ inline uint32_t range_begin(uint32_t n, uint32_t i, uint32_t G) {
+    return n * i / G;
 }
 
 // Largest CTA index whose range starts at or before block x.
-__device__ __forceinline__ uint32_t cta_of(uint64_t n, uint32_t G, uint64_t x) {
-    uint32_t i = (uint32_t)(x * G / n);
+__device__ __forceinline__ uint32_t cta_of(uint32_t n, uint32_t G, uint32_t x) {
+    uint32_t i = x * G / n;
     while (i + 1 < G && range_begin(n, i + 1, G) <= x) ++i;
     while (i > 0 && range_begin(n, i, G) > x) --i;
     return i;
@@ -175,8 +177,20 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
 
     const uint32_t tid = threadIdx.x;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
-    const uint64_t NB = (uint64_t)a.n_slabs * nb;
+    const uint32_t NB = a.n_slabs * nb;
     const uint32_t x0 = range_begin(NB, cta, G), x1 = range_begin(NB, cta + 1, G);
+    // Only the first and last slab of the range can be shared with other
+    // CTAs; resolve their owners once, here.
+    const uint32_t j_first = x0 / nb, j_last = (x1 - 1) / nb;
+    uint32_t own_lo[2] = {cta, cta}, own_hi[2] = {cta, cta};  // [first slab, last slab]
+    if (j_first * nb < x0 || (j_first + 1) * nb > x1) {
+        own_lo[0] = cta_of(NB, G, j_first * nb);
+        own_hi[0] = cta_of(NB, G, j_first * nb + nb - 1);
+    }
+    if (j_last != j_first && (j_last + 1) * nb > x1) {
+        own_lo[1] = cta;
+        own_hi[1] = cta_of(NB, G, j_last * nb + nb - 1);
+    }
     const uint32_t n_stages = (x1 - x0 + a.stage_blocks - 1) / a.stage_blocks;
 
     if (tid == 0) {
@@ -320,8 +334,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
                     if (lane < 16)
 #pragma unroll
                         for (uint32_t w = 0; w < NW; ++w) v += rb[w * 16 + lane];
-                    const uint32_t c_first = cta_of(NB, G, jb);
-                    const uint32_t c_last = cta_of(NB, G, jb + nb - 1);
+                    const uint32_t which = j == j_first ? 0 : 1;
+                    const uint32_t c_first = (j == j_first || j == j_last) ? own_lo[which] : cta;
+                    const uint32_t c_last = (j == j_first || j == j_last) ? own_hi[which] : cta;
                     bool finish = c_first == c_last;
                     if (!finish) {
                         float* pp = a.part + ((size_t)j * a.max_parts) * 16;

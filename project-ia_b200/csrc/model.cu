@@ -205,7 +205,6 @@ static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStr
     AttnArgs a{};
     a.q = s->q;
     a.kv_layer = kv_layer;
-    a.scores = s->scores;
     a.cmax = s->cmax;
     a.opart = s->opart;
     a.lpart = s->lpart;
@@ -216,13 +215,23 @@ static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStr
     a.n_kv_heads = s->cfg.n_kv_heads;
     a.max_seq = s->cfg.max_seq_len;
     a.n_chunks = s->n_chunks;
+    a.chunk_alloc = (s->cfg.max_seq_len + s->n_chunks - 1) / s->n_chunks;
     a.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
+    const size_t smem = attn_smem_bytes(s->cfg.n_heads / s->cfg.n_kv_heads, a.chunk_alloc);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(attn_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    });
+    if (smem > 64 * 1024) return cudaErrorInvalidValue;
     // cooperative: every CTA of the grid is resident, so the per-head
     // barriers inside the kernel cannot wait on an unscheduled CTA; no
     // programmatic overlap with the QKV GEMV before it for the same reason
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(s->cfg.n_kv_heads, s->n_chunks);
     cfg.blockDim = dim3(ATT_THREADS);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;

@@ -87,6 +87,7 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     p.stage_blocks = stage_blocks;
     p.n_stage = n_stage;
     p.grid = (uint32_t)std::min<uint64_t>(NB, (uint64_t)per_sm * sms);
+    if (NB * p.grid >= (1ull << 32)) return false;  // the kernel's range math is 32-bit
     const uint64_t per_cta = std::max<uint64_t>(1, NB / p.grid);
     p.max_parts = (uint32_t)((nb + per_cta - 1) / per_cta + 2);
     p.smem = gemv_smem_bytes(nb, stage_blocks, n_stage);
