@@ -59,6 +59,9 @@ static constexpr int GEMV_CONSUMER_WARPS = 8;
 static constexpr int GEMV_THREADS = GEMV_CONSUMER_WARPS * 32 + 32;
 static constexpr uint32_t GEMV_BLOCK_BYTES = 320;  // one (slab, block) unit
 static constexpr uint32_t GEMV_BFRAG_BYTES = 96;   // x limb fragments of a block (12 lanes)
+static constexpr int GEMV_XREGS = 8;               // input float4s per thread per batch
+// An RMSNorm prologue needs the whole input in one register batch.
+static constexpr uint32_t GEMV_MAX_NORM_K = GEMV_CONSUMER_WARPS * 32 * GEMV_XREGS * 4;
 
 struct GemvArgs {
     const uint8_t* w;          // packed slab tiles
@@ -228,50 +231,101 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
     const uint32_t lane = tid & 31, warp = tid >> 5;
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)a.step->token * a.K;
+    // All input loads are issued at once (float4, registers); a serial loop
+    // of dependent L2 loads here would delay the whole stream by microseconds.
+    // Thread tid holds float4 number tid + T*r; 8 consecutive threads hold
+    // one 32-element Q4 block.
+    constexpr int NR = GEMV_XREGS;
+    const uint32_t n4 = a.K / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
+    const float4* g4 = reinterpret_cast<const float4*>(a.norm_w);
     float r_norm = 1.0f;
-    if (a.norm_w) {
-        // upstream rmsnorm.c: mean of squares, rsqrt + one Newton step
-        float ss = 0.0f;
-        for (uint32_t i = tid; i < a.K; i += T) ss = __fmaf_rn(xs[i], xs[i], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) rms_part[warp] = ss;
-        asm volatile("bar.sync 1, %0;" ::"r"(T));
-        float tot = 0.0f;
-        for (uint32_t i = 0; i < NW; ++i) tot += rms_part[i];
-        float me = __fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps);
-        float r0 = __fdiv_rn(1.0f, __fsqrt_rn(me));
-        float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0, r0)));
-        r_norm = __fmul_rn(__fmul_rn(r0, tm), 0.5f);
-    }
-    if (a.x_copy && cta == 0)
-        for (uint32_t i = tid; i < a.K; i += T) a.x_copy[i] = xs[i];
-    // Fixed-point limbs of every input block: warp w handles blocks w, w+8, ...
-    // lane j holds element 32b + j.  B fragment of lane L = g*4 + t (g < 3 =
-    // limb): word 0 = limb g of k 4t..4t+3, word 1 = limb g of k 16+4t..16+4t+3.
-    for (uint32_t b = warp; b < nb; b += NW) {
-        float xv = xs[(size_t)b * 32 + lane];
-        if (a.norm_w) xv = __fmul_rn(__fmul_rn(xv, r_norm), a.norm_w[(size_t)b * 32 + lane]);
-        const float m = warp_max(fabsf(xv));
-        int e = 0;
-        if (m > 0.0f) frexpf(m, &e);
-        const int sh = 22 - e;
-        const int X = __float2int_rn(ldexpf(xv, sh));  // |X| < 2^22
-        const int c8 = (int)(int8_t)(X & 0xFF);
-        const int X1 = (X - c8) >> 8;
-        const int b8 = (int)(int8_t)(X1 & 0xFF);
-        const int a8 = (X1 - b8) >> 8;
-        int sx = X;
+    for (uint32_t base = 0; base < n4; base += T * NR) {
+        float4 xv[NR], gv[NR];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
-        uint8_t* bf = bfrag + (size_t)b * GEMV_BFRAG_BYTES;
-        const uint32_t t = (lane & 15) >> 2, wd = lane >> 4, by = lane & 3;
-        const uint32_t off = t * 8 + wd * 4 + by;
-        bf[0 * 32 + off] = (uint8_t)a8;
-        bf[1 * 32 + off] = (uint8_t)b8;
-        bf[2 * 32 + off] = (uint8_t)c8;
-        if (lane == 0) {
-            const float f = ldexpf(1.0f, -sh);
-            fsc[b] = make_float2(f, f * (-8.0f * (float)sx));
+        for (int r = 0; r < NR; ++r) {
+            const uint32_t i = base + tid + T * r;
+            xv[r] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            gv[r] = (g4 && i < n4) ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (a.x_copy && cta == 0) {
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const uint32_t i = base + tid + T * r;
+                if (i < n4) reinterpret_cast<float4*>(a.x_copy)[i] = xv[r];
+            }
+        }
+        if (a.norm_w && base == 0) {
+            // upstream rmsnorm.c: mean of squares, rsqrt + one Newton step
+            // (the host only pairs a norm with K <= T*NR*4, one batch)
+            float ss = 0.0f;
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                ss = __fmaf_rn(xv[r].x, xv[r].x, ss);
+                ss = __fmaf_rn(xv[r].y, xv[r].y, ss);
+                ss = __fmaf_rn(xv[r].z, xv[r].z, ss);
+                ss = __fmaf_rn(xv[r].w, xv[r].w, ss);
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) rms_part[warp] = ss;
+            asm volatile("bar.sync 1, %0;" ::"r"(T));
+            float tot = 0.0f;
+            for (uint32_t i = 0; i < NW; ++i) tot += rms_part[i];
+            float me = __fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps);
+            float r0 = __fdiv_rn(1.0f, __fsqrt_rn(me));
+            float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0, r0)));
+            r_norm = __fmul_rn(__fmul_rn(r0, tm), 0.5f);
+        }
+        // Fixed-point limbs: B fragment of lane L = g*4 + t (g < 3 = limb):
+        // word 0 = limb g of k 4t..4t+3, word 1 = limb g of k 16+4t..16+4t+3.
+        // This thread's float4 is k = 4*sub..4*sub+3 of its block, i.e.
+        // t = sub % 4, word = sub / 4: one 32-bit store per limb.
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            const uint32_t i = base + tid + T * r;
+            if (base + T * r >= n4) break;  // uniform: whole warp past the end
+            float4 v = xv[r];
+            if (a.norm_w) {
+                v.x = __fmul_rn(__fmul_rn(v.x, r_norm), gv[r].x);
+                v.y = __fmul_rn(__fmul_rn(v.y, r_norm), gv[r].y);
+                v.z = __fmul_rn(__fmul_rn(v.z, r_norm), gv[r].z);
+                v.w = __fmul_rn(__fmul_rn(v.w, r_norm), gv[r].w);
+            }
+            float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            int e = 0;
+            if (m > 0.0f) frexpf(m, &e);
+            const int sh = 22 - e;
+            const int X[4] = {__float2int_rn(ldexpf(v.x, sh)), __float2int_rn(ldexpf(v.y, sh)),
+                              __float2int_rn(ldexpf(v.z, sh)), __float2int_rn(ldexpf(v.w, sh))};
+            uint32_t la = 0, lb = 0, lc = 0;
+            int sx = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int c8 = (int)(int8_t)(X[q] & 0xFF);
+                const int X1 = (X[q] - c8) >> 8;
+                const int b8 = (int)(int8_t)(X1 & 0xFF);
+                const int a8 = (X1 - b8) >> 8;
+                la |= (uint32_t)(a8 & 0xFF) << (8 * q);
+                lb |= (uint32_t)(b8 & 0xFF) << (8 * q);
+                lc |= (uint32_t)(c8 & 0xFF) << (8 * q);
+                sx += X[q];
+            }
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+            if (i < n4) {
+                const uint32_t b = i / 8, sub = i % 8;
+                uint32_t* bf = reinterpret_cast<uint32_t*>(bfrag + (size_t)b * GEMV_BFRAG_BYTES);
+                const uint32_t w = (sub % 4) * 2 + sub / 4;  // 32-bit word within a limb's 32 B
+                bf[0 * 8 + w] = la;
+                bf[1 * 8 + w] = lb;
+                bf[2 * 8 + w] = lc;
+                if (sub == 0) {
+                    const float f = ldexpf(1.0f, -sh);
+                    fsc[b] = make_float2(f, f * (-8.0f * (float)sx));
+                }
+            }
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
@@ -298,6 +352,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
             const uint32_t seg_end = min(sb1, jb + nb);
             // this warp's blocks of the segment: (b - jb) % NW == warp
             uint32_t b = seg + ((warp + NW - (seg - jb) % NW) % NW);
+#ifdef QB200_GEMV_NO_COMPUTE  // experiment builds only: stream without arithmetic
+            b = seg_end;
+#endif
             for (; b < seg_end; b += NW) {
                 const uint8_t* blk = stage + (size_t)(b - sb0) * GEMV_BLOCK_BYTES;
                 const uint2 q = *reinterpret_cast<const uint2*>(blk + lane * 8);

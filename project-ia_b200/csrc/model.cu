@@ -35,7 +35,7 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     s->kvd = c.n_kv_heads * s->hd;
     const uint32_t G = c.n_heads / c.n_kv_heads;
     if (!(s->hd == 32 || s->hd == 64 || s->hd == 128) || G > (uint32_t)ATT_MAXG ||
-        c.n_heads % c.n_kv_heads || c.max_seq_len == 0)
+        c.n_heads % c.n_kv_heads || c.max_seq_len == 0 || D > GEMV_MAX_NORM_K || D % 4)
         return Q_ERR_INVALID_CONFIG;
     if (!plan_gemv(D + 2 * s->kvd, D, s->p_qkv) || !plan_gemv(D, D, s->p_wo) ||
         !plan_gemv(2 * H, D, s->p_gu) || !plan_gemv(D, H, s->p_down))

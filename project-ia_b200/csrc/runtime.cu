@@ -68,7 +68,10 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     const uint64_t NB = (uint64_t)n_slabs * nb;
     const int sms = device_sms();
     const size_t fixed = gemv_smem_bytes(nb, 0, 0);
-    uint32_t stage_blocks = 64;  // 20 KB stages
+#ifndef QB200_GEMV_STAGE_BLOCKS
+#define QB200_GEMV_STAGE_BLOCKS 64  // 20 KB stages
+#endif
+    uint32_t stage_blocks = QB200_GEMV_STAGE_BLOCKS;
     uint32_t per_sm = 2, n_stage = 0;
     // two CTAs per SM (the next kernel's CTA also fits under programmatic
     // dependent launch) when a >= 2-stage ring fits in ~113 KB, else one
