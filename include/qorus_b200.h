@@ -80,6 +80,16 @@ q_error_code q_b200_decode_greedy(q_llama_model* model, q_context* ctx, uint32_t
 q_error_code q_b200_decode_loop(q_llama_model* model, q_context* ctx, uint32_t first_token,
                                 uint32_t pos, uint32_t n_steps, uint32_t* out_tokens, int sync);
 
+/* Profiling: one greedy decode step (as q_b200_decode_greedy) replayed from
+ * a separately captured graph whose kernels stamp %globaltimer.  For each
+ * kernel in launch order, out[3i..3i+2] = earliest CTA entry, earliest end
+ * of its programmatic-dependency wait, latest exit (ns).  At most
+ * max_kernels kernels are reported; *n_kernels receives the count.
+ * Stands beside upstream's benchmark timing (tools/benchmark.c:22-50). */
+q_error_code q_b200_profile_step(q_llama_model* model, q_context* ctx, uint32_t token,
+                                 uint32_t pos, uint64_t* out, uint32_t max_kernels,
+                                 uint32_t* n_kernels);
+
 /* Device logits of the last forward / decode step ([vocab] fp32). */
 const float* q_b200_device_logits(q_context* ctx);
 

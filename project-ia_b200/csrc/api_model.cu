@@ -311,6 +311,40 @@ q_error_code q_b200_decode_loop(q_llama_model* model, q_context* ctx, uint32_t f
     return Q_OK;
 }
 
+q_error_code q_b200_profile_step(q_llama_model* model, q_context* ctx, uint32_t token,
+                                 uint32_t pos, uint64_t* out, uint32_t max_kernels,
+                                 uint32_t* n_kernels) {
+    if (!model || !ctx || !out || !n_kernels) return Q_ERR_INVALID_ARG;
+    if (token >= model->config.vocab_size || pos >= model->config.max_seq_len) return Q_ERR_INVALID_ARG;
+    DevState* s = nullptr;
+    q_error_code rc = ready(model, ctx, &s);
+    if (rc != Q_OK) return rc;
+    if ((rc = capture_trace_graph(ctx, s)) != Q_OK) return rc;
+    std::vector<unsigned long long> buf((size_t)s->trace_slots * 4);
+    for (size_t i = 0; i < s->trace_slots; ++i) {
+        buf[4 * i] = buf[4 * i + 1] = ~0ull;
+        buf[4 * i + 2] = buf[4 * i + 3] = 0ull;
+    }
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    Q_CUDA(cudaMemcpy(s->trace_buf, buf.data(), buf.size() * 8, cudaMemcpyHostToDevice));
+    StepParams* hp = &s->h_step[0];
+    hp->token = token;
+    hp->pos = pos;
+    hp->n_row = hp->valid = pos + 1;
+    Q_CUDA(cudaMemcpyAsync(s->step, hp, sizeof *hp, cudaMemcpyHostToDevice, s->stream));
+    Q_CUDA(cudaMemsetAsync(s->tok_count, 0, 4, s->stream));
+    Q_CUDA(cudaGraphLaunch(s->g_trace, s->stream));
+    g_kernel_launches.fetch_add(s->kernels_full);
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    if ((rc = check_device_status("q_b200_profile_step")) != Q_OK) return rc;
+    Q_CUDA(cudaMemcpy(buf.data(), s->trace_buf, buf.size() * 8, cudaMemcpyDeviceToHost));
+    const uint32_t n = std::min(max_kernels, s->trace_slots);
+    for (uint32_t i = 0; i < n; ++i)
+        for (int k = 0; k < 3; ++k) out[3 * i + k] = buf[4 * i + k];
+    *n_kernels = n;
+    return Q_OK;
+}
+
 q_error_code q_b200_decode_greedy(q_llama_model* model, q_context* ctx, uint32_t token,
                                   uint32_t pos, uint32_t* next_token) {
     if (!next_token) return Q_ERR_INVALID_ARG;

@@ -49,6 +49,7 @@ struct AttnArgs {
     uint32_t n_heads, n_kv_heads, max_seq, n_chunks;  // n_chunks = NC (grid.y)
     uint32_t chunk_alloc;    // >= ceil(max_seq / NC): shared scores per head
     float scale;             // 1/sqrtf(hd), computed on the host like upstream
+    unsigned long long* trace;  // step-trace slot (null: off)
 };
 
 __host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t chunk_alloc) {
@@ -96,8 +97,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
     __shared__ float gmax[ATT_MAXG];
     __shared__ __align__(16) float4 ored[PL][ATT_MAXG][VL];
     __shared__ float lsum[ATT_MAXG];
+    if (threadIdx.x == 0) trace_mark(a.trace, 0);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(a.trace, 1);
     const uint32_t h = blockIdx.x, c = blockIdx.y;
     const uint32_t G = a.n_heads / a.n_kv_heads;
     const uint32_t valid = a.step->valid, N = a.step->n_row;
@@ -296,6 +299,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
             ctr[2] = 0u;
             __threadfence();
         }
+        trace_mark(a.trace, 2);
     }
 }
 

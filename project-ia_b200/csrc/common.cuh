@@ -103,6 +103,23 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- step tracing ---------------------------------------------------------------
+// A traced kernel gets a slot of 4 u64: [0] earliest CTA entry, [1] earliest
+// end of the programmatic-dependency wait, [2] latest exit (ns, %globaltimer).
+// Slots start as {~0, ~0, 0, 0}; a null slot disables tracing (one branch).
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void trace_mark(unsigned long long* slot, int which) {
+    if (slot == nullptr) return;
+    if (which < 2) atomicMin(slot + which, gtimer());
+    else atomicMax(slot + 2, gtimer());
+}
+
 // ---- loads / misc -------------------------------------------------------------
 
 __device__ __forceinline__ float4 ldg_stream_f4(const float4* p) {

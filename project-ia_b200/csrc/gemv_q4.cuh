@@ -86,6 +86,7 @@ struct GemvArgs {
     const float* rope_sin;
     float* kv_layer;           // [n_kv][max_seq][2*hd] of this layer
     uint32_t hd, q_rows, kv_rows, max_seq;
+    unsigned long long* trace;  // step-trace slot (null: off)
 };
 
 // Shared memory: ring | bfrag[nb][96] | fsc[nb] float2 | red[2][8][16] | bars | misc
@@ -204,6 +205,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
         fence_mbar_init();
     }
     __syncthreads();
+    if (tid == 0) trace_mark(a.trace, 0);
     pdl_trigger();
 
     if (tid >= T) {
@@ -228,6 +230,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
 
     // ---- consumers: input prologue -------------------------------------------
     pdl_wait();
+    if (tid == 0) trace_mark(a.trace, 1);
     const uint32_t lane = tid & 31, warp = tid >> 5;
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)a.step->token * a.K;
@@ -422,6 +425,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (tid == 0) trace_mark(a.trace, 2);
 }
 
 // Repack upstream AoS Q4_0 blocks ([M][nb] x 20 B) into slab tiles.

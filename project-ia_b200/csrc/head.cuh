@@ -27,6 +27,7 @@ struct HeadArgs {
     uint32_t row_base;         // global index of row 0 (vocab split)
     float* logits;             // [rows]
     unsigned long long* best;  // argmax key (null: none)
+    unsigned long long* trace; // step-trace slot (null: off)
 };
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
@@ -39,8 +40,10 @@ __global__ void __launch_bounds__(HEAD_THREADS) lm_head_kernel(const HeadArgs a)
     extern __shared__ __align__(16) float xs[];  // [K]
     __shared__ float part[HEAD_THREADS / 32];
     __shared__ unsigned long long wbest[HEAD_THREADS / 32];
+    if (threadIdx.x == 0) trace_mark(a.trace, 0);
     pdl_trigger();
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(a.trace, 1);
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float r = 1.0f;
     if (a.norm_w) {
@@ -108,13 +111,17 @@ __global__ void __launch_bounds__(HEAD_THREADS) lm_head_kernel(const HeadArgs a)
             }
         }
     }
-    if (!a.best) return;
+    if (!a.best) {
+        if (tid == 0) trace_mark(a.trace, 2);
+        return;
+    }
     if (lane == 0) wbest[warp] = best;
     __syncthreads();
     if (tid == 0) {
         unsigned long long b = 0ull;
         for (int i = 0; i < HEAD_THREADS / 32; ++i) b = wbest[i] > b ? wbest[i] : b;
         if (b) atomicMax(a.best, b);
+        trace_mark(a.trace, 2);
     }
 }
 
@@ -127,12 +134,15 @@ struct AdvanceArgs {
     uint32_t* token_count;     // index into token_out
     uint32_t token_cap;
     uint32_t* last_token;      // most recent argmax
+    unsigned long long* trace; // step-trace slot (null: off)
 };
 
 __global__ void advance_kernel(const AdvanceArgs a) {
+    if (threadIdx.x == 0) trace_mark(a.trace, 0);
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    trace_mark(a.trace, 1);
     const unsigned long long k = *a.best;
     const uint32_t tok = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
     *a.last_token = tok;
@@ -146,6 +156,7 @@ __global__ void advance_kernel(const AdvanceArgs a) {
     s.valid = s.pos + 1;
     *a.step = s;
     *a.best = 0ull;
+    trace_mark(a.trace, 2);
 }
 
 }  // namespace qb200

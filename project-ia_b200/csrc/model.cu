@@ -201,6 +201,14 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
 
 // ---- graph capture ------------------------------------------------------------------
 
+// Next step-trace slot while capturing the traced graph, else null.
+static unsigned long long* take_slot(DevState* s) {
+    if (!s->tr_next) return nullptr;
+    unsigned long long* p = s->tr_next;
+    s->tr_next += 4;
+    return p;
+}
+
 static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStream_t st) {
     AttnArgs a{};
     a.q = s->q;
@@ -209,6 +217,7 @@ static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStr
     a.opart = s->opart;
     a.lpart = s->lpart;
     a.sync = s->ticket;
+    a.trace = take_slot(s);
     a.out = s->att;
     a.step = s->step;
     a.n_heads = s->cfg.n_heads;
@@ -270,6 +279,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         g.q_rows = D;
         g.kv_rows = s->kvd;
         g.max_seq = c.max_seq_len;
+        g.trace = take_slot(s);
         e = launch_gemv(s->p_qkv, g, s->gemv_scratch, st, l != 0);
         if (e == cudaSuccess) e = enqueue_attention(s, kvl, st);
         if (e != cudaSuccess) break;
@@ -280,6 +290,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         o.y = s->x;
         o.resid = s->x;
         o.epi = EPI_RESID;
+        o.trace = take_slot(s);
         e = launch_gemv(s->p_wo, o, s->gemv_scratch, st, true);
         if (e != cudaSuccess) break;
         GemvArgs u{};
@@ -290,6 +301,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         u.eps = c.rms_norm_eps;
         u.y = s->h;
         u.epi = EPI_SILU;
+        u.trace = take_slot(s);
         e = launch_gemv(s->p_gu, u, s->gemv_scratch, st, true);
         if (e != cudaSuccess) break;
         GemvArgs d{};
@@ -299,6 +311,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         d.y = s->x;
         d.resid = s->x;
         d.epi = EPI_RESID;
+        d.trace = take_slot(s);
         e = launch_gemv(s->p_down, d, s->gemv_scratch, st, true);
     }
     return e;
@@ -315,6 +328,7 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     h.row_base = 0;
     h.logits = s->logits;
     h.best = s->best;
+    h.trace = take_slot(s);
     static std::once_flag once;
     std::call_once(once, [] {
         cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
@@ -331,6 +345,7 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     a.token_count = s->tok_count;
     a.token_cap = s->tok_cap;
     a.last_token = s->last_tok;
+    a.trace = take_slot(s);
     return launch_ex(advance_kernel, dim3(1), dim3(32), 0, st, true, a);
 }
 
@@ -355,11 +370,27 @@ static q_error_code capture(DevState* s, float* kv, bool with_head, cudaGraphExe
     return cuda_ok(e, "graph instantiate") ? Q_OK : Q_ERR_INVALID_ARG;
 }
 
+q_error_code capture_trace_graph(q_context* ctx, DevState* s) {
+    if (s->g_trace) return Q_OK;
+    const uint32_t slots = s->cfg.n_layers * 6 + 4;
+    if (!s->trace_buf &&
+        !cuda_ok(cudaMalloc(&s->trace_buf, (size_t)slots * 4 * sizeof(unsigned long long)), "trace buf"))
+        return Q_ERR_ALLOC_FAILED;
+    s->trace_slots = slots;
+    s->tr_next = s->trace_buf;
+    uint64_t nk = 0;
+    q_error_code rc = capture(s, (float*)ctx->kv_buffer, true, &s->g_trace, &nk);
+    s->trace_slots = (uint32_t)((s->tr_next - s->trace_buf) / 4);
+    s->tr_next = nullptr;
+    return rc;
+}
+
 q_error_code ensure_graphs(q_context* ctx, DevState* s) {
     if (s->g_full && s->graph_kv == ctx->kv_buffer) return Q_OK;
     if (s->g_body) cudaGraphExecDestroy(s->g_body);
     if (s->g_full) cudaGraphExecDestroy(s->g_full);
-    s->g_body = s->g_full = nullptr;
+    if (s->g_trace) cudaGraphExecDestroy(s->g_trace);
+    s->g_body = s->g_full = s->g_trace = nullptr;
     float* kv = (float*)ctx->kv_buffer;
     q_error_code rc = capture(s, kv, false, &s->g_body, &s->kernels_body);
     if (rc == Q_OK) rc = capture(s, kv, true, &s->g_full, &s->kernels_full);

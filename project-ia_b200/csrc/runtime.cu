@@ -72,13 +72,19 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
 #define QB200_GEMV_STAGE_BLOCKS 64  // 20 KB stages
 #endif
     uint32_t stage_blocks = QB200_GEMV_STAGE_BLOCKS;
-    uint32_t per_sm = 2, n_stage = 0;
+#ifndef QB200_GEMV_PER_SM
+#define QB200_GEMV_PER_SM 2
+#endif
+#ifndef QB200_GEMV_MAX_STAGES
+#define QB200_GEMV_MAX_STAGES 8
+#endif
+    uint32_t per_sm = QB200_GEMV_PER_SM, n_stage = 0;
     // two CTAs per SM (the next kernel's CTA also fits under programmatic
     // dependent launch) when a >= 2-stage ring fits in ~113 KB, else one
     for (; per_sm >= 1; --per_sm) {
         const size_t budget = per_sm == 2 ? 113 * 1024 : 220 * 1024;
         if (budget <= fixed) continue;
-        n_stage = (uint32_t)std::min<size_t>(per_sm == 2 ? 4 : 8,
+        n_stage = (uint32_t)std::min<size_t>(QB200_GEMV_MAX_STAGES,
                                              (budget - fixed) / (stage_blocks * GEMV_BLOCK_BYTES));
         if (n_stage >= 2) break;
     }
@@ -193,7 +199,10 @@ void* dev_arena_alloc(DevState* s, size_t bytes) {
 void free_model(DevState* s) {
     if (s->g_body) cudaGraphExecDestroy(s->g_body);
     if (s->g_full) cudaGraphExecDestroy(s->g_full);
-    s->g_body = s->g_full = nullptr;
+    if (s->g_trace) cudaGraphExecDestroy(s->g_trace);
+    if (s->trace_buf) cudaFree(s->trace_buf);
+    s->trace_buf = nullptr;
+    s->g_body = s->g_full = s->g_trace = nullptr;
     s->graph_kv = nullptr;
     for (void* p : s->weight_allocs) cudaFree(p);
     s->weight_allocs.clear();

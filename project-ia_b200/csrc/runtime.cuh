@@ -111,6 +111,11 @@ struct DevState {
     void* graph_kv = nullptr;
     cudaGraphExec_t g_body = nullptr, g_full = nullptr;
     uint64_t kernels_body = 0, kernels_full = 0;
+    // step tracing: a third graph whose kernels stamp per-kernel times
+    cudaGraphExec_t g_trace = nullptr;
+    unsigned long long* trace_buf = nullptr;   // [slots][4] device
+    unsigned long long* tr_next = nullptr;     // capture cursor (null: untraced)
+    uint32_t trace_slots = 0;
 };
 
 DevState* state_of(const q_context* ctx, bool create);
@@ -119,6 +124,7 @@ void* dev_arena_alloc(DevState* s, size_t bytes);
 
 q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* model);
 q_error_code ensure_graphs(q_context* ctx, DevState* s);
+q_error_code capture_trace_graph(q_context* ctx, DevState* s);
 q_error_code check_device_status(const char* where);
 void free_model(DevState* s);
 

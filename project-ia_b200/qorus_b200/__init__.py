@@ -129,6 +129,7 @@ _SIGS = {
     "q_b200_stream": (_vp, [_vp]),
     "q_b200_decode_greedy": (_i, [_vp, _vp, _u32, _u32, _vp]),
     "q_b200_decode_loop": (_i, [_vp, _vp, _u32, _u32, _u32, _vp, _i]),
+    "q_b200_profile_step": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
     "q_b200_device_logits": (_vp, [_vp]),
     "q_b200_q4_packed_bytes": (_sz, [_u32, _u32]),
     "q_b200_q4_pack": (_i, [_vp, _u32, _u32, _vp, _vp]),
@@ -231,6 +232,14 @@ class Model:
                                      ptr(out), 1 if sync else 0), "q_b200_decode_loop")
         return out
 
+    def profile_step(self, token: int, pos: int) -> np.ndarray:
+        """[kernel][entry, wait-end, exit] globaltimer ns of one traced decode step."""
+        out = np.zeros((1024, 3), np.uint64)
+        n = C.c_uint32()
+        check(lib.q_b200_profile_step(C.byref(self.model), C.byref(self.ctx), token, pos, ptr(out),
+                                      1024, C.byref(n)), "q_b200_profile_step")
+        return out[: n.value]
+
     def kv_write(self, host: np.ndarray, offset: int = 0) -> None:
         check(lib.q_b200_kv_write(C.byref(self.ctx), offset, ptr(host), host.nbytes), "kv_write")
 
@@ -251,3 +260,4 @@ class Model:
             self.close()
         except Exception:
             pass
+

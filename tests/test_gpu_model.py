@@ -140,3 +140,29 @@ def test_llama8b_shapes_decode_over_prefilled_cache(llama8b_2layer):
     kv_close(kv, orc.kv)
     dev.close()
     orc.close()
+
+
+def test_profile_step_stamps_and_result(tiny_path, golden):
+    """The traced step writes the same KV rows as an untraced one and stamps
+    every kernel of the step in launch order."""
+    dev = Q.Model(tiny_path)
+    prompt = golden["tiny_prompt"]
+    tok = int(np.argmax(dev.forward(prompt, 0)))
+    kv0 = np.zeros(Q.kv_bytes(dev.cfg) // 4, np.float32)
+    dev.kv_read(kv0)
+    st = dev.profile_step(tok, len(prompt))
+    L = dev.cfg.n_layers
+    assert st.shape == (L * 5 + 2, 3)  # per layer: qkv, attention, wo, gate/up, down; head, advance
+    assert (st[:, 0] <= st[:, 1]).all() and (st[:, 1] <= st[:, 2]).all()
+    assert (st[1:, 2] >= st[:-1, 2]).all()
+    kv_traced = np.zeros_like(kv0)
+    dev.kv_read(kv_traced)
+    dev.kv_write(kv0)
+    nxt = C.c_uint32()
+    Q.check(Q.lib.q_b200_decode_greedy(C.byref(dev.model), C.byref(dev.ctx), tok, len(prompt),
+                                       C.byref(nxt)), "decode_greedy")
+    assert nxt.value == golden["tiny_tokens"][1]
+    kv_plain = np.zeros_like(kv0)
+    dev.kv_read(kv_plain)
+    assert np.array_equal(kv_traced, kv_plain)
+    dev.close()
