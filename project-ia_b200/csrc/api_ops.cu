@@ -261,3 +261,15 @@ void q_dequantize_q4_0_block_avx2_public(const q_block_q4_0* block, float* outpu
 }
 
 }  // extern "C"
+
+#ifdef QB200_GEMV_PHASES
+extern "C" int q_b200_dbg_gemv_phases(void* host, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(host, qb200::g_gemv_phase, bytes);
+}
+#endif
+
+#ifdef QB200_ATTN_PHASES
+extern "C" int q_b200_dbg_attn_phases(void* host, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(host, qb200::g_attn_phase, bytes);
+}
+#endif

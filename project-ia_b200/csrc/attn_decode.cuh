@@ -80,6 +80,16 @@ __device__ __forceinline__ void head_barrier(uint32_t* ctr, uint32_t target) {
     __syncthreads();
 }
 
+#ifdef QB200_ATTN_PHASES  // experiment builds only: per-CTA phase timestamps
+__device__ unsigned long long g_attn_phase[1024 * 8];
+#define ATTN_PHASE(i)                                                                         \
+    do {                                                                                      \
+        if (threadIdx.x == 0) g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + (i)] = gtimer(); \
+    } while (0)
+#else
+#define ATTN_PHASE(i) ((void)0)
+#endif
+
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnArgs a) {
     constexpr int LPP = HD / 16;                 // lanes per K row (16 floats each)
@@ -101,6 +111,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) trace_mark(a.trace, 1);
+    ATTN_PHASE(0);
     const uint32_t h = blockIdx.x, c = blockIdx.y;
     const uint32_t G = a.n_heads / a.n_kv_heads;
     const uint32_t valid = a.step->valid, N = a.step->n_row;
@@ -126,6 +137,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
     for (uint32_t i = tid; i < G * HD; i += ATT_THREADS)
         qs[i / HD][i % HD] = a.q[(size_t)(h * G) * HD + i];
     __syncthreads();
+    ATTN_PHASE(1);
 
     // ---- phase 1: scores + chunk max ------------------------------------------
     {
@@ -183,7 +195,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
             a.cmax[(size_t)(h * G + tid) * a.n_chunks + c] = m;
         }
     }
+    ATTN_PHASE(2);
     head_barrier(ctr + 0, n_act);
+    ATTN_PHASE(3);
 
     // ---- phase 2: exponentials (upstream index rule) + partial P.V -------------
     if (warp < G) {
@@ -252,7 +266,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
         }
         if (tid < G) a.lpart[(size_t)(h * G + tid) * a.n_chunks + c] = lsum[tid];
     }
+    ATTN_PHASE(4);
     head_barrier(ctr + 1, n_act);
+    ATTN_PHASE(5);
 
     // ---- phase 3: this CTA's slice of the outputs --------------------------------
     // The partials sit in L2; chunk sums are spread over lanes so every load
@@ -301,6 +317,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
         }
         trace_mark(a.trace, 2);
     }
+    ATTN_PHASE(6);
 }
 
 }  // namespace qb200

@@ -4,7 +4,7 @@
 // (transaction-count barriers), cp.async.bulk (the 1-D TMA engine: global ->
 // shared copies that complete on an mbarrier), programmatic dependent launch
 // (griddepcontrol) and streaming loads.  Every spin wait is bounded: after
-// Q_SPIN_LIMIT polls it records an error code in the device status word and
+// Q_WAIT_NS (or Q_SPIN_LIMIT polls) it records an error code in the device status word and
 // gives up, so a lost transaction never hangs the GPU.
 #pragma once
 
@@ -13,6 +13,9 @@
 
 #ifndef Q_SPIN_LIMIT
 #define Q_SPIN_LIMIT (1u << 26)
+#endif
+#ifndef Q_WAIT_NS
+#define Q_WAIT_NS 2000000000ull  // 2 s
 #endif
 
 // Device status word (one per library load); 0 = OK.  Kernels write a code
@@ -30,6 +33,13 @@ enum : uint32_t {
 __device__ uint32_t g_qdev_status = 0;
 
 __device__ __forceinline__ void qdev_fail(uint32_t code) { atomicCAS(&g_qdev_status, 0u, code); }
+
+// Global nanosecond timer (bounds every wait in wall time).
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -69,10 +79,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`; false (and an error code) on timeout.
+// try_wait with a suspend-time hint: the warp sleeps in hardware until the
+// phase completes or about `ns` nanoseconds pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`; false (and an error code) after
+// Q_WAIT_NS of wall time or Q_SPIN_LIMIT polls, whichever comes first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
-    for (uint32_t i = 0; i < Q_SPIN_LIMIT; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    for (uint32_t i = 0; i < Q_SPIN_LIMIT; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+        if (gtimer() - t0 > Q_WAIT_NS) break;
+    }
     qdev_fail(code);
     return false;
 }
@@ -107,12 +136,6 @@ __device__ __forceinline__ void pdl_trigger() {
 // A traced kernel gets a slot of 4 u64: [0] earliest CTA entry, [1] earliest
 // end of the programmatic-dependency wait, [2] latest exit (ns, %globaltimer).
 // Slots start as {~0, ~0, 0, 0}; a null slot disables tracing (one branch).
-
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 __device__ __forceinline__ void trace_mark(unsigned long long* slot, int which) {
     if (slot == nullptr) return;

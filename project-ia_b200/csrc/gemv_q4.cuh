@@ -70,6 +70,7 @@ struct GemvArgs {
     uint32_t stage_blocks;     // blocks per ring stage
     uint32_t n_stage;          // ring depth
     uint32_t max_parts;        // CTAs that can share one slab
+    uint32_t red_slabs;        // slab sums a CTA holds in shared memory between reductions
     const float* x;            // input vector, or the embedding table if gather
     const StepParams* step;    // per-step scalars (token, pos)
     uint32_t gather;           // non-zero: x row = x + step->token * K (embedding)
@@ -89,11 +90,12 @@ struct GemvArgs {
     unsigned long long* trace;  // step-trace slot (null: off)
 };
 
-// Shared memory: ring | bfrag[nb][96] | fsc[nb] float2 | red[2][8][16] | bars | misc
+// Shared memory: ring | bfrag[nb][96] | fsc[nb] float2 | red[red_slabs][8][16] | bars | misc
 __host__ __device__ inline size_t gemv_smem_bytes(uint32_t nb, uint32_t stage_blocks,
-                                                  uint32_t n_stage) {
+                                                  uint32_t n_stage, uint32_t red_slabs) {
     return (size_t)n_stage * stage_blocks * GEMV_BLOCK_BYTES + (size_t)nb * GEMV_BFRAG_BYTES +
-           (size_t)nb * 8 + 2 * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 + 64 * 4 + 128;
+           (size_t)nb * 8 + (size_t)red_slabs * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 +
+           64 * 4 + 128;
 }
 
 // CTA i owns blocks [n*i/G, n*(i+1)/G) of the slab-major block sequence
@@ -120,7 +122,7 @@ __device__ __forceinline__ void rope_pair(float v0, float v1, const float* ct,
 
 __device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
@@ -166,6 +168,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uin
     }
 }
 
+#ifdef QB200_GEMV_PHASES  // experiment builds only: per-CTA phase timestamps
+__device__ unsigned long long g_gemv_phase[2048 * 8];
+#define GEMV_PHASE(i, v) (g_gemv_phase[blockIdx.x * 8 + (i)] = (v))
+#else
+#define GEMV_PHASE(i, v) ((void)0)
+#endif
+
 __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t NW = GEMV_CONSUMER_WARPS, T = NW * 32;
@@ -174,10 +183,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
     uint8_t* ring = smem;
     uint8_t* bfrag = ring + (size_t)a.n_stage * stage_bytes;
     float2* fsc = reinterpret_cast<float2*>(bfrag + (size_t)nb * GEMV_BFRAG_BYTES);
-    float* red = reinterpret_cast<float*>(fsc + nb);             // [2][NW][16]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * NW * 16);
+    float* red = reinterpret_cast<float*>(fsc + nb);             // [red_slabs][NW][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)a.red_slabs * NW * 16);
     uint64_t* empty = full + 8;
-    float* rms_part = reinterpret_cast<float*>(empty + 8);
+    float* rms_part = reinterpret_cast<float*>(empty + 8);   // [NW]
 
     const uint32_t tid = threadIdx.x;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
@@ -206,23 +215,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
     }
     __syncthreads();
     if (tid == 0) trace_mark(a.trace, 0);
+    if (tid == 0) GEMV_PHASE(0, gtimer());
     pdl_trigger();
 
     if (tid >= T) {
         // ---- producer warp: stream this CTA's block range -------------------
         if (tid == T) {
             const uint64_t pol = l2_evict_first_policy();
-            for (uint32_t k = 0; k < n_stages; ++k) {
-                const uint32_t s = k % a.n_stage;
-                if (k >= a.n_stage &&
-                    !mbar_wait(&empty[s], ((k / a.n_stage) & 1) ^ 1, QDEV_WAIT_EMPTY_TIMEOUT))
-                    break;
-                const uint32_t b0 = x0 + k * a.stage_blocks;
+            uint32_t s = 0, ph = 0;  // ring slot and its phase parity
+            for (uint32_t k = 0, b0 = x0; k < n_stages; ++k, b0 += a.stage_blocks) {
+                if (k >= a.n_stage && !mbar_wait(&empty[s], ph ^ 1, QDEV_WAIT_EMPTY_TIMEOUT)) break;
                 const uint32_t n = min(a.stage_blocks, x1 - b0);
                 mbar_arrive_expect_tx(&full[s], n * GEMV_BLOCK_BYTES);
                 bulk_g2s(ring + (size_t)s * stage_bytes, a.w + (size_t)b0 * GEMV_BLOCK_BYTES,
                          n * GEMV_BLOCK_BYTES, &full[s], pol);
+                if (++s == a.n_stage) {
+                    s = 0;
+                    ph ^= 1;
+                }
             }
+            GEMV_PHASE(5, gtimer());
         }
         pdl_wait();  // every thread waits: the grid ends after its predecessor
         return;
@@ -231,6 +243,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
     // ---- consumers: input prologue -------------------------------------------
     pdl_wait();
     if (tid == 0) trace_mark(a.trace, 1);
+    if (tid == 0) GEMV_PHASE(1, gtimer());
     const uint32_t lane = tid & 31, warp = tid >> 5;
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)a.step->token * a.K;
@@ -297,11 +310,19 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
             float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
             for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            int e = 0;
-            if (m > 0.0f) frexpf(m, &e);
-            const int sh = 22 - e;
-            const int X[4] = {__float2int_rn(ldexpf(v.x, sh)), __float2int_rn(ldexpf(v.y, sh)),
-                              __float2int_rn(ldexpf(v.z, sh)), __float2int_rn(ldexpf(v.w, sh))};
+            // Grid 2^-sh with sh = 22 - e, m = f 2^e (f in [0.5, 1)): for a
+            // normal m, e = E - 126 with E its biased exponent field.  A
+            // subnormal m uses E = 1 (a coarser grid, still |X| <= 2^22), an
+            // all-zero block any E.  v 2^sh is formed as two exact
+            // power-of-two products (sh spans -106..147); an intermediate
+            // can only lose bits when the final value rounds to 0 anyway.
+            const int E = m > 0.0f ? max((int)(__float_as_uint(m) >> 23), 1) : 126;
+            const int sh = 148 - E, s1 = sh >> 1, s2 = sh - s1;
+            const float p1 = __int_as_float((s1 + 127) << 23), p2 = __int_as_float((s2 + 127) << 23);
+            const int X[4] = {__float2int_rn(__fmul_rn(__fmul_rn(v.x, p1), p2)),
+                              __float2int_rn(__fmul_rn(__fmul_rn(v.y, p1), p2)),
+                              __float2int_rn(__fmul_rn(__fmul_rn(v.z, p1), p2)),
+                              __float2int_rn(__fmul_rn(__fmul_rn(v.w, p1), p2))};
             uint32_t la = 0, lb = 0, lc = 0;
             int sx = 0;
 #pragma unroll
@@ -325,107 +346,181 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
                 bf[1 * 8 + w] = lb;
                 bf[2 * 8 + w] = lc;
                 if (sub == 0) {
-                    const float f = ldexpf(1.0f, -sh);
+                    // 2^-sh = 2^(E-148): normal for E >= 22, else the
+                    // subnormal 2^(E+1) * 2^-149
+                    const float f = __uint_as_float(E >= 22 ? (uint32_t)(E - 21) << 23
+                                                            : 1u << (E + 1));
                     fsc[b] = make_float2(f, f * (-8.0f * (float)sx));
                 }
             }
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
+    if (tid == 0) GEMV_PHASE(2, gtimer());
+#ifdef QB200_GEMV_PHASES
+    unsigned long long ph_wait = 0, ph_flush = 0;
+#endif
 
     // ---- main loop ---------------------------------------------------------------
     const uint32_t g = lane >> 2, t = lane & 3;
-    // limb weights: lane t=0 holds columns (a, b) -> a*256 + b, scaled by 256;
-    // t=1 holds (c, 0) plus the -8*sum(X) correction; t=2,3 hold zeros.
-    const int m0 = t == 0 ? 256 : (t == 1 ? 1 : 0);
+    // D fragment of lane (g, t): rows g and g+8, columns 2t, 2t+1.  Columns
+    // 0..2 are the limbs (a, b, c); lanes t >= 2 and column 3 see whatever
+    // B lanes 12..31 load (their rows of the limb table, reused) and are
+    // cancelled by zero weights.  t = 0: p = 256*D_a + D_b, weight 256 f;
+    // t = 1: p = D_c, weight f, plus the -8*sum(X) correction.
+    const int m0 = t == 0 ? 256 : 1;
     const int m1 = t == 0 ? 1 : 0;
     const float wt = t == 0 ? 256.0f : (t == 1 ? 1.0f : 0.0f);
-    const bool has_corr = t == 1;
-    const uint32_t zero_lane = lane >= 12;
+    const float ct = t == 1 ? 1.0f : 0.0f;
+    const uint32_t ring_off = 0;
+    const uint32_t bfrag_off = (uint32_t)(bfrag - smem) + (lane % 12) * 8;
+    const uint32_t fsc_off = (uint32_t)(reinterpret_cast<uint8_t*>(fsc) - smem);
+    // One block: bytes at smem + q (weights, lane part), + sq (scales of
+    // rows g, g+8), + bq (limb fragment), + fq (grid factor, correction).
+    auto block_terms = [&](uint32_t q_off, uint32_t b_off, uint32_t f_off, float& u0, float& u1,
+                           float2& sc) {
+        const uint2 q = *reinterpret_cast<const uint2*>(smem + q_off);
+        sc = *reinterpret_cast<const float2*>(smem + q_off + (256 + g * 8 - lane * 8));
+        const uint2 bv = *reinterpret_cast<const uint2*>(smem + b_off);
+        const float2 fz = *reinterpret_cast<const float2*>(smem + f_off);
+        int d[4];
+#ifdef QB200_GEMV_NO_MMA  // experiment builds only
+        d[0] = q.x ^ bv.x; d[1] = q.y ^ bv.y; d[2] = (q.x >> 4) ^ bv.y; d[3] = (q.y >> 4) ^ bv.x;
+#else
+        mma_u8s8(d, q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, (q.x >> 4) & 0x0F0F0F0Fu,
+                 (q.y >> 4) & 0x0F0F0F0Fu, bv.x, bv.y);
+#endif
+        const float fw = fz.x * wt;
+        const float fc = fz.y * ct;
+        u0 = __fmaf_rn((float)(d[0] * m0 + d[1] * m1), fw, fc);
+        u1 = __fmaf_rn((float)(d[2] * m0 + d[3] * m1), fw, fc);
+    };
+    // Slab sums wait in red[] (per warp) and are reduced by the whole CTA
+    // every red_slabs slabs and at the end: warp w finishes slabs w, w+NW, ...
+    // of the batch (cross-CTA parts through the ticket, then the epilogue).
+    const uint32_t RS = a.red_slabs;
+    uint32_t jl = 0, j_batch = j_first;
+    auto reduce_batch = [&](uint32_t cnt) {
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        for (uint32_t r = warp; r < cnt; r += NW) {
+            const uint32_t j = j_batch + r;
+            float v = 0.0f;
+            if (lane < 16)
+#pragma unroll
+                for (uint32_t w = 0; w < NW; ++w) v += red[(r * NW + w) * 16 + lane];
+            const uint32_t c_first = j == j_first ? own_lo[0] : (j == j_last ? own_lo[1] : cta);
+            const uint32_t c_last = j == j_first ? own_hi[0] : (j == j_last ? own_hi[1] : cta);
+            bool finish = c_first == c_last;
+            if (!finish) {
+                float* pp = a.part + ((size_t)j * a.max_parts) * 16;
+                if (lane < 16) pp[(cta - c_first) * 16 + lane] = v;
+                __threadfence();
+                uint32_t last = 0;
+                if (lane == 0) last = atomicAdd(&a.ticket[j], 1u) == c_last - c_first ? 1u : 0u;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    v = 0.0f;
+                    if (lane < 16)
+                        for (uint32_t p = 0; p <= c_last - c_first; ++p) v += __ldcg(&pp[p * 16 + lane]);
+                    if (lane == 0) a.ticket[j] = 0u;
+                    finish = true;
+                }
+            }
+            if (finish && lane < 16) gemv_epilogue(a, j, lane, v);
+        }
+        j_batch += cnt;
+        jl = 0;
+    };
     float acc0 = 0.0f, acc1 = 0.0f;
-    uint32_t rbuf = 0;
-    for (uint32_t k = 0; k < n_stages; ++k) {
-        const uint32_t s = k % a.n_stage;
-        const bool ok = mbar_wait(&full[s], (k / a.n_stage) & 1, QDEV_WAIT_FULL_TIMEOUT);
-        const uint8_t* stage = ring + (size_t)s * stage_bytes;
-        const uint32_t sb0 = x0 + k * a.stage_blocks;
+    // running ring slot / parity and current slab (no divisions per stage)
+    uint32_t s = 0, ph = 0, j = j_first, jb = j_first * nb;
+    for (uint32_t k = 0, sb0 = x0; k < n_stages; ++k, sb0 += a.stage_blocks) {
+#ifdef QB200_GEMV_PHASES
+        const unsigned long long pw0 = gtimer();
+#endif
+        mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
+#ifdef QB200_GEMV_PHASES
+        ph_wait += gtimer() - pw0;
+        if (k == 0 && tid == 0) GEMV_PHASE(3, gtimer());
+#endif
         const uint32_t sb1 = min(sb0 + a.stage_blocks, x1);
         for (uint32_t seg = sb0; seg < sb1;) {
-            const uint32_t j = seg / nb, jb = j * nb;
             const uint32_t seg_end = min(sb1, jb + nb);
             // this warp's blocks of the segment: (b - jb) % NW == warp
-            uint32_t b = seg + ((warp + NW - (seg - jb) % NW) % NW);
+            const uint32_t b = seg + ((warp + NW - (seg - jb) % NW) % NW);
+            int n = b < seg_end ? (int)((seg_end - b + NW - 1) / NW) : 0;
 #ifdef QB200_GEMV_NO_COMPUTE  // experiment builds only: stream without arithmetic
-            b = seg_end;
+            n = 0;
 #endif
-            for (; b < seg_end; b += NW) {
-                const uint8_t* blk = stage + (size_t)(b - sb0) * GEMV_BLOCK_BYTES;
-                const uint2 q = *reinterpret_cast<const uint2*>(blk + lane * 8);
-                const uint32_t kb = b - jb;
-                uint2 bv = make_uint2(0u, 0u);
-                if (!zero_lane) bv = *reinterpret_cast<const uint2*>(bfrag + (size_t)kb * GEMV_BFRAG_BYTES + lane * 8);
-                int d[4];
-                mma_u8s8(d, q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, (q.x >> 4) & 0x0F0F0F0Fu,
-                         (q.y >> 4) & 0x0F0F0F0Fu, bv.x, bv.y);
-                const float2 sc = *reinterpret_cast<const float2*>(blk + 256 + g * 8);
-                const float2 fz = fsc[kb];
-                const float fw = fz.x * wt;
-                const float fc = has_corr ? fz.y : 0.0f;
-                const float p0 = (float)(d[0] * m0 + d[1] * m1);
-                const float p1 = (float)(d[2] * m0 + d[3] * m1);
-                acc0 = __fmaf_rn(sc.x, __fmaf_rn(p0, fw, fc), acc0);
-                acc1 = __fmaf_rn(sc.y, __fmaf_rn(p1, fw, fc), acc1);
+            uint32_t qo = ring_off + s * stage_bytes + (b - sb0) * GEMV_BLOCK_BYTES + lane * 8;
+            uint32_t bo = bfrag_off + (b - jb) * GEMV_BFRAG_BYTES;
+            uint32_t fo = fsc_off + (b - jb) * 8;
+            constexpr uint32_t QS = NW * GEMV_BLOCK_BYTES, BS = NW * GEMV_BFRAG_BYTES, FS = NW * 8;
+            // four independent blocks per step, accumulated in block order
+            for (; n >= 4; n -= 4, qo += 4 * QS, bo += 4 * BS, fo += 4 * FS) {
+                float u[4][2];
+                float2 sc[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    block_terms(qo + i * QS, bo + i * BS, fo + i * FS, u[i][0], u[i][1], sc[i]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc0 = __fmaf_rn(sc[i].x, u[i][0], acc0);
+                    acc1 = __fmaf_rn(sc[i].y, u[i][1], acc1);
+                }
+            }
+            for (; n > 0; --n, qo += QS, bo += BS, fo += FS) {
+                float u0, u1;
+                float2 sc;
+                block_terms(qo, bo, fo, u0, u1, sc);
+                acc0 = __fmaf_rn(sc.x, u0, acc0);
+                acc1 = __fmaf_rn(sc.y, u1, acc1);
             }
             if (seg_end == jb + nb || seg_end == x1) {
-                // flush slab j: limbs (quad) -> warps (smem) -> CTA parts (global)
+#ifdef QB200_GEMV_PHASES
+                const unsigned long long pf0 = gtimer();
+#endif
+                // slab j done for this warp: limbs (quad) -> red[jl][warp]
                 acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
                 acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
                 acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
                 acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-                float* rb = red + rbuf * NW * 16;
                 if (t == 0) {
-                    rb[warp * 16 + g] = ok ? acc0 : 0.0f;
-                    rb[warp * 16 + g + 8] = ok ? acc1 : 0.0f;
+                    red[(jl * NW + warp) * 16 + g] = acc0;
+                    red[(jl * NW + warp) * 16 + g + 8] = acc1;
                 }
                 acc0 = acc1 = 0.0f;
-                asm volatile("bar.sync 1, %0;" ::"r"(T));
-                if (warp == 0) {
-                    float v = 0.0f;
-                    if (lane < 16)
-#pragma unroll
-                        for (uint32_t w = 0; w < NW; ++w) v += rb[w * 16 + lane];
-                    const uint32_t which = j == j_first ? 0 : 1;
-                    const uint32_t c_first = (j == j_first || j == j_last) ? own_lo[which] : cta;
-                    const uint32_t c_last = (j == j_first || j == j_last) ? own_hi[which] : cta;
-                    bool finish = c_first == c_last;
-                    if (!finish) {
-                        float* pp = a.part + ((size_t)j * a.max_parts) * 16;
-                        if (lane < 16) pp[(cta - c_first) * 16 + lane] = v;
-                        __threadfence();
-                        uint32_t last = 0;
-                        if (lane == 0)
-                            last = atomicAdd(&a.ticket[j], 1u) == c_last - c_first ? 1u : 0u;
-                        last = __shfl_sync(0xffffffffu, last, 0);
-                        if (last) {
-                            __threadfence();
-                            v = 0.0f;
-                            if (lane < 16)
-                                for (uint32_t p = 0; p <= c_last - c_first; ++p)
-                                    v += __ldcg(&pp[p * 16 + lane]);
-                            if (lane == 0) a.ticket[j] = 0u;
-                            finish = true;
-                        }
-                    }
-                    if (finish && lane < 16) gemv_epilogue(a, j, lane, v);
+                if (++jl == RS) {
+                    reduce_batch(RS);
+                    asm volatile("bar.sync 1, %0;" ::"r"(T));  // red[] free again
                 }
-                rbuf ^= 1;
+#ifdef QB200_GEMV_PHASES
+                ph_flush += gtimer() - pf0;
+#endif
+            }
+            if (seg_end == jb + nb) {
+                ++j;
+                jb += nb;
             }
             seg = seg_end;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == a.n_stage) {
+            s = 0;
+            ph ^= 1;
+        }
     }
+    if (jl) reduce_batch(jl);
     if (tid == 0) trace_mark(a.trace, 2);
+#ifdef QB200_GEMV_PHASES
+    if (tid == 0) {
+        GEMV_PHASE(4, gtimer());
+        GEMV_PHASE(6, ph_wait);
+        GEMV_PHASE(7, ph_flush);
+    }
+#endif
 }
 
 // Repack upstream AoS Q4_0 blocks ([M][nb] x 20 B) into slab tiles.

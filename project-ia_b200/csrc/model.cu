@@ -335,8 +335,13 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     });
     const uint32_t grid = std::max<uint32_t>(
         1, std::min<uint32_t>(2 * device_sms(), (s->cfg.vocab_size + 15) / 16));
-    cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS),
-                              (size_t)s->cfg.dim * 4, st, true, h);
+    // The grid-stride row loop gives every CTA the same work, so CTAs must
+    // spread evenly over the SMs.  Launched early under programmatic
+    // dependent launch, the scheduler would otherwise stack many CTAs on the
+    // first SMs the previous kernel frees; the shared-memory request caps
+    // residency at two CTAs per SM.
+    const size_t smem = std::max<size_t>((size_t)s->cfg.dim * 4, 96 * 1024);
+    cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), smem, st, true, h);
     if (e != cudaSuccess) return e;
     AdvanceArgs a{};
     a.step = s->step;

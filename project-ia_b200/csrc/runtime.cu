@@ -67,7 +67,6 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     if (n_slabs > GemvPlan::kTicketWords) return false;
     const uint64_t NB = (uint64_t)n_slabs * nb;
     const int sms = device_sms();
-    const size_t fixed = gemv_smem_bytes(nb, 0, 0);
 #ifndef QB200_GEMV_STAGE_BLOCKS
 #define QB200_GEMV_STAGE_BLOCKS 64  // 20 KB stages
 #endif
@@ -81,7 +80,14 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     uint32_t per_sm = QB200_GEMV_PER_SM, n_stage = 0;
     // two CTAs per SM (the next kernel's CTA also fits under programmatic
     // dependent launch) when a >= 2-stage ring fits in ~113 KB, else one
+    uint32_t red_slabs = 1;
     for (; per_sm >= 1; --per_sm) {
+        // slabs one CTA's range touches (at most), held in shared memory
+        // between CTA-wide reductions (capped: longer ranges reduce in batches)
+        const uint64_t grid = std::min<uint64_t>(NB, (uint64_t)per_sm * sms);
+        const uint64_t range = (NB + grid - 1) / grid;
+        red_slabs = (uint32_t)std::min<uint64_t>(32, (range + nb - 1) / nb + 1);
+        const size_t fixed = gemv_smem_bytes(nb, 0, 0, red_slabs);
         const size_t budget = per_sm == 2 ? 113 * 1024 : 220 * 1024;
         if (budget <= fixed) continue;
         n_stage = (uint32_t)std::min<size_t>(QB200_GEMV_MAX_STAGES,
@@ -99,7 +105,8 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     if (NB * p.grid >= (1ull << 32)) return false;  // the kernel's range math is 32-bit
     const uint64_t per_cta = std::max<uint64_t>(1, NB / p.grid);
     p.max_parts = (uint32_t)((nb + per_cta - 1) / per_cta + 2);
-    p.smem = gemv_smem_bytes(nb, stage_blocks, n_stage);
+    p.red_slabs = red_slabs;
+    p.smem = gemv_smem_bytes(nb, stage_blocks, n_stage, red_slabs);
     p.packed_bytes = (size_t)NB * GEMV_BLOCK_BYTES;
     return true;
 }
@@ -112,6 +119,7 @@ cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, void* scratch, cudaStream
     a.stage_blocks = p.stage_blocks;
     a.n_stage = p.n_stage;
     a.max_parts = p.max_parts;
+    a.red_slabs = p.red_slabs;
     a.ticket = reinterpret_cast<uint32_t*>(scratch);
     a.part = reinterpret_cast<float*>(a.ticket + GemvPlan::kTicketWords);
     static std::once_flag once;

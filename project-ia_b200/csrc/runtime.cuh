@@ -36,7 +36,7 @@ cudaStream_t op_stream();  // stream for the kernel-level entry points
 
 struct GemvPlan {
     uint32_t M = 0, K = 0, n_slabs = 0, nb = 0, stage_blocks = 0, n_stage = 0, max_parts = 0;
-    uint32_t grid = 0;
+    uint32_t grid = 0, red_slabs = 0;
     size_t smem = 0, packed_bytes = 0;
     // Scratch layout, shared by every plan: a fixed ticket area of
     // kTicketWords uint32 (zero between launches: each finisher resets its

@@ -50,12 +50,13 @@ def test_gemv_host_api_vs_upstream(golden):
         close(y, golden[key[:-1] + "y"])
 
 
-def _device_gemv(torch, M, K, seed):
+def _device_gemv(torch, M, K, seed, x=None):
     nblk = M * K // 32
     w = np.zeros(nblk * 20, np.uint8)
     Q.lib.q_b200_fill_q4(Q.ptr(w), nblk, seed, 11, 0, 0.001, 0.01, 0)
-    x = np.zeros(K, np.float32)
-    Q.lib.q_b200_fill_normal(Q.ptr(x), K, seed, 12, 0, 0.0, 1.0, 0)
+    if x is None:
+        x = np.zeros(K, np.float32)
+        Q.lib.q_b200_fill_normal(Q.ptr(x), K, seed, 12, 0, 0.0, 1.0, 0)
     dw = torch.from_numpy(w).cuda()
     packed = torch.empty(Q.lib.q_b200_q4_packed_bytes(M, K), dtype=torch.uint8, device="cuda")
     dx = torch.from_numpy(x).cuda()
@@ -75,6 +76,31 @@ def _device_gemv(torch, M, K, seed):
 def test_gemv_device_vs_oracle(torch, M, K):
     dev, ref = _device_gemv(torch, M, K, seed=M + K)
     close(dev, ref)
+
+
+@pytest.mark.parametrize("scale", [1e-33, 1e-30, 1e20, 1e-41, 0.0])
+def test_gemv_input_magnitudes(torch, scale):
+    """The fixed-point input grid follows each block's exponent: tiny, huge,
+    subnormal and all-zero inputs, with every third block zero and one block
+    holding a single non-zero value."""
+    M, K = 512, 4096
+    x = np.zeros(K, np.float32)
+    Q.lib.q_b200_fill_normal(Q.ptr(x), K, 5, 12, 0, 0.0, 1.0, 0)
+    x = (x.astype(np.float64) * scale).astype(np.float32)
+    x.reshape(-1, 32)[::3] = 0.0
+    x.reshape(-1, 32)[1, 1:] = 0.0
+    dev, ref = _device_gemv(torch, M, K, 9, x)
+    assert np.isfinite(dev).all()
+    if scale == 0.0:
+        assert (dev == 0).all()
+        return
+    if scale < 1e-38:
+        # subnormal inputs: upstream's own fp32 products keep only a few bits
+        # here, so only the magnitude is compared
+        assert np.abs(dev).max() <= 1e-36 and np.abs(ref).max() <= 1e-36
+        return
+    unit = max(float(np.abs(ref).max()), np.finfo(np.float32).tiny)
+    close(dev / unit, ref / unit)
 
 
 def test_gemv_f32_vs_oracle(torch):
