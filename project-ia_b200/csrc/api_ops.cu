@@ -118,10 +118,7 @@ q_error_code q_b200_gemv_f32(const float* d_w, uint32_t M, uint32_t K, const flo
     h.rows = M;
     h.K = K;
     h.logits = d_y;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    });
+    Q_CUDA(ensure_smem_attr((const void*)lm_head_kernel, 160 * 1024));
     const uint32_t grid = std::max<uint32_t>(1, std::min<uint32_t>(2 * device_sms(), (M + 15) / 16));
     Q_CUDA(launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), (size_t)K * 4,
                      (cudaStream_t)stream, false, h));

@@ -227,13 +227,12 @@ static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStr
     a.chunk_alloc = (s->cfg.max_seq_len + s->n_chunks - 1) / s->n_chunks;
     a.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
     const size_t smem = attn_smem_bytes(s->cfg.n_heads / s->cfg.n_kv_heads, a.chunk_alloc);
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(attn_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-        cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-        cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    });
     if (smem > 64 * 1024) return cudaErrorInvalidValue;
+    for (const void* k : {(const void*)attn_decode_kernel<32>, (const void*)attn_decode_kernel<64>,
+                          (const void*)attn_decode_kernel<128>}) {
+        const cudaError_t e = ensure_smem_attr(k, 64 * 1024);
+        if (e != cudaSuccess) return e;
+    }
     // cooperative: every CTA of the grid is resident, so the per-head
     // barriers inside the kernel cannot wait on an unscheduled CTA; no
     // programmatic overlap with the QKV GEMV before it for the same reason
@@ -329,10 +328,10 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     h.logits = s->logits;
     h.best = s->best;
     h.trace = take_slot(s);
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    });
+    {
+        const cudaError_t e = ensure_smem_attr((const void*)lm_head_kernel, 160 * 1024);
+        if (e != cudaSuccess) return e;
+    }
     const uint32_t grid = std::max<uint32_t>(
         1, std::min<uint32_t>(2 * device_sms(), (s->cfg.vocab_size + 15) / 16));
     // The grid-stride row loop gives every CTA the same work, so CTAs must

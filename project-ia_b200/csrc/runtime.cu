@@ -2,6 +2,7 @@
 // registry of libqorus_b200.so.
 #include <cmath>
 #include <cstdio>
+#include <set>
 
 #include "runtime.cuh"
 
@@ -35,10 +36,27 @@ int device_sms() {
 }
 
 cudaStream_t op_stream() {
-    static std::once_flag once;
-    static cudaStream_t s = nullptr;
-    std::call_once(once, [] { cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking); });
+    static std::mutex mu;
+    static std::unordered_map<int, cudaStream_t> streams;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    cudaStream_t& s = streams[dev];
+    if (!s) cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
     return s;
+}
+
+cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({kernel, dev})) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({kernel, dev});
+    return e;
 }
 
 q_error_code check_device_status(const char* where) {
@@ -122,10 +140,8 @@ cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, void* scratch, cudaStream
     a.red_slabs = p.red_slabs;
     a.ticket = reinterpret_cast<uint32_t*>(scratch);
     a.part = reinterpret_cast<float*>(a.ticket + GemvPlan::kTicketWords);
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(gemv_q4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    });
+    const cudaError_t e = ensure_smem_attr((const void*)gemv_q4_kernel, 220 * 1024);
+    if (e != cudaSuccess) return e;
     return launch_ex(gemv_q4_kernel, dim3(p.grid), dim3(GEMV_THREADS), p.smem, s, pdl, a);
 }
 

@@ -25,7 +25,10 @@ bool cuda_ok(cudaError_t e, const char* where);
 const char* last_error_cstr();
 extern std::atomic<uint64_t> g_kernel_launches;
 int device_sms();
-cudaStream_t op_stream();  // stream for the kernel-level entry points
+cudaStream_t op_stream();  // stream for the kernel-level entry points (per device)
+// cudaFuncAttributeMaxDynamicSharedMemorySize = bytes for `kernel` on the
+// current device (set once per kernel and device).
+cudaError_t ensure_smem_attr(const void* kernel, int bytes);
 
 #define Q_CUDA(call)                                                    \
     do {                                                                \
