@@ -104,6 +104,16 @@ q_error_code q_b200_q4_pack(const q_block_q4_0* d_src, uint32_t M, uint32_t K,
 q_error_code q_b200_gemv_q4(const void* d_packed, uint32_t M, uint32_t K,
                             const float* d_x, float* d_y, void* stream);
 
+/* Same GEMV as q_b200_gemv_q4, for callers that may not allocate device
+ * memory: no cudaMalloc/cudaFree ever; split-slab scratch is a fixed 2 MiB
+ * device array of the library.  The first call on a device (device current)
+ * resolves that array and must precede any stream capture meant to hold the
+ * launch; shapes needing more scratch return Q_ERR_INVALID_SIZE; calls that
+ * can overlap on one device race on the shared scratch and must be
+ * serialised by the caller.  No counterpart in the reference. */
+q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M, uint32_t K,
+                                    const float* d_x, float* d_y, void* stream);
+
 /* FP32 GEMV y[M] = W[M,K] x[K] (the LM head of upstream
  * src/models/model.c:1821-1844, dot order of src/ops/avx2/matmul_fp32.c). */
 q_error_code q_b200_gemv_f32(const float* d_w, uint32_t M, uint32_t K,

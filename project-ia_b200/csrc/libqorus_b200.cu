@@ -6,3 +6,4 @@
 #include "api.cu"
 #include "api_model.cu"
 #include "api_ops.cu"
+#include "api_noalloc.cu"

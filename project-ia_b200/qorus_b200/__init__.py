@@ -134,6 +134,7 @@ _SIGS = {
     "q_b200_q4_packed_bytes": (_sz, [_u32, _u32]),
     "q_b200_q4_pack": (_i, [_vp, _u32, _u32, _vp, _vp]),
     "q_b200_gemv_q4": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
+    "q_b200_gemv_q4_noalloc": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_gemv_f32": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_kernel_launches": (_u64, []),
     "q_b200_last_error": (C.c_char_p, []),
