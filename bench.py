@@ -130,6 +130,11 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes (read + write) of one gate/up launch, from an ncu capture of
+# `bench.py --only gemv` (profiles/gemv_q4_gate_up_28672x4096.txt).
+GEMV_GU_TRAFFIC = 74_420_992
+
+
 def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
     """Dominant kernel: the fused gate/up Q4_0 GEMV shape of the 8B layer
     (28672 x 4096), launched back to back over 4 distinct weight sets (294 MB
@@ -165,7 +170,9 @@ def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
     return {"kernel": "gemv_q4_kernel (fused gate/up 28672x4096)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "us_per_launch": round(us, 2),
-            "bytes_per_launch": bytes_launch, "traffic": None, "peak_source": "of measured"}
+            "bytes_per_launch": bytes_launch, "traffic": GEMV_GU_TRAFFIC,
+            "traffic_source": "ncu dram__bytes_read+write of one launch, profiles/gemv_q4_gate_up_28672x4096.txt",
+            "peak_source": "of measured"}
 
 
 def cpu_reference_decode(path: str, cfg, steps: int, threads: int):
