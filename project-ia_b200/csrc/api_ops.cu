@@ -269,4 +269,7 @@ extern "C" int q_b200_dbg_gemv_phases(void* host, size_t bytes) {
 extern "C" int q_b200_dbg_attn_phases(void* host, size_t bytes) {
     return (int)cudaMemcpyFromSymbol(host, qb200::g_attn_phase, bytes);
 }
+extern "C" int q_b200_dbg_attn_stages(void* host, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(host, qb200::g_attn_stage, bytes);
+}
 #endif

@@ -1,4 +1,5 @@
-// attn_decode.cuh — split-KV decode attention over the HBM KV cache (sm_100a).
+// attn_decode.cuh — split-KV GQA decode attention, one thread-block cluster
+// per KV head (sm_100a).
 //
 // Replaces the upstream attention block of src/models/model.c:1226-1438:
 // per query head, scores = (q . k_j) * (1/sqrt(hd)) (q_matmul_f32_avx2 +
@@ -7,215 +8,300 @@
 // positions 0..valid-1 as the graph intends.  The softmax keeps upstream's
 // numerics: the global row max first, then the polynomial exp on elements
 // i < 8*floor(N/8) and expf on the tail (all expf when N < 8), where N is
-// the row length of the upstream call (pos + seq_len).  That exp is not
-// multiplicative, so the row max is global before any exponential (no
-// online-softmax rescaling).
+// the row length of the upstream call (pos + seq_len); masked positions
+// contribute exactly 0 upstream and are skipped here.  That exp is clamped,
+// hence not multiplicative, so the row max is global before any exponential
+// (no online-softmax rescaling).
 //
 // Cache layout (upstream get_kv_cache_ptr, model.c:700-740):
 // [layer][kv_head][max_seq][K(hd) | V(hd)] fp32.
 //
-// One kernel, grid (n_kv_heads, NC), launched cooperatively so all CTAs are
-// co-resident.  The G query heads of a KV head share its CTAs, so every K/V
-// row is read once.  The valid positions are split over the first n_act <=
-// NC CTAs of each head; a CTA issues all K and V loads of its chunk (in
-// sub-chunks of 64 positions) before it needs them, keeps its scores in
-// shared memory, and passes three phases:
-//   1. scores (HD/16 lanes per position), chunk max -> global | head barrier
-//   2. global max, exponentials, partial P.V and sums -> global | head barrier
-//   3. each CTA combines a slice of the G*HD outputs.
-// Barriers are atomic counters per head with bounded spins; the last CTA of
-// a head resets that head's counters for the next launch.
+// Grid (CS, n_kv_heads), cluster (CS, 1, 1): the CS CTAs of a cluster share
+// one KV head and split its valid positions into CS contiguous chunks; the
+// G query heads of that KV head ride along, so every K/V row is read once.
+// In each CTA a producer warp streams the chunk's K rows and then its V rows
+// through a shared-memory ring — one tiled TMA copy per stage through a
+// tensor map over the whole cache (box = SP rows x hd floats at the cache's
+// row stride; this GPU's own memory, no multicast) — while 8 consumer warps
+//   1. compute scores into shared memory and the chunk max,
+//   | cluster barrier: every CTA reads all chunk maxima over distributed
+//   | shared memory (same order everywhere, so the same global max),
+//   2. turn scores into exponentials (upstream's index rule), sum them, and
+//      accumulate partial P.V from the V rows (already streaming in),
+//   | cluster barrier,
+//   3. finish a 1/CS slice of the G*hd outputs: sum the CS partials (CTA
+//      order) and multiply by 1/L.
+//   | cluster barrier (no CTA leaves while others read its shared memory).
+// Rows older than the current position do not depend on the previous kernel
+// and are copied before the programmatic-dependency wait; the current row
+// (written by the QKV epilogue just before) is copied after it.
 #pragma once
+
+#include <cuda.h>  // CUtensorMap
 
 #include "common.cuh"
 #include "gemv_q4.cuh"
 
 namespace qb200 {
 
-static constexpr int ATT_THREADS = 256;
-static constexpr int ATT_MAXG = 8;        // query heads per KV head supported
-static constexpr int ATT_MIN_CHUNK = 32;  // positions per CTA before using more CTAs
-static constexpr int ATT_SUB = 64;        // positions per register-resident sub-chunk
+static constexpr int ATT_CWARPS = 8;                           // consumer warps
+static constexpr int ATT_THREADS = ATT_CWARPS * 32 + 32;       // + producer warp
+static constexpr int ATT_MAXG = 8;                             // query heads per KV head
+static constexpr uint32_t ATT_STAGE_BYTES = 16384;             // one ring slot
+static constexpr uint32_t ATT_MAX_SLOTS = 8;
 
 struct AttnArgs {
     const float* q;          // [n_heads][hd] rotated queries
-    const float* kv_layer;   // this layer's cache base
-    float* cmax;             // [n_heads][NC]
-    float* opart;            // [n_heads][NC][hd]
-    float* lpart;            // [n_heads][NC]
-    uint32_t* sync;          // [n_kv_heads][4] counters, zero between launches
+    uint32_t layer;          // cache plane z = layer * n_kv_heads + kv head
     float* out;              // [n_heads][hd]
     const StepParams* step;
-    uint32_t n_heads, n_kv_heads, max_seq, n_chunks;  // n_chunks = NC (grid.y)
-    uint32_t chunk_alloc;    // >= ceil(max_seq / NC): shared scores per head
+    uint32_t n_heads, n_kv_heads, max_seq;
+    uint32_t chunk_alloc;    // >= ceil(max_seq / CS), a multiple of 4: scores per query head
+    uint32_t slots;          // ring depth (2..ATT_MAX_SLOTS)
     float scale;             // 1/sqrtf(hd), computed on the host like upstream
     unsigned long long* trace;  // step-trace slot (null: off)
 };
 
-__host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t chunk_alloc) {
-    return (size_t)G * chunk_alloc * 4;
+// ring[slots][16 KB] | sc[G][chunk_alloc] | ored[PG][G][hd] | opart[G][hd]
+__host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t hd, uint32_t chunk_alloc,
+                                                  uint32_t slots) {
+    const uint32_t PG = (ATT_CWARPS * 32) / (hd / 4);
+    return (size_t)slots * ATT_STAGE_BYTES + (size_t)G * chunk_alloc * 4 + (size_t)PG * G * hd * 4 +
+           (size_t)G * hd * 4;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Whole-warp calls only (.aligned): each reconverges its warp first.
+__device__ __forceinline__ void cluster_arrive() {
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    __syncwarp();
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Tiled TMA load of box (x, y, z) of a 3-D tensor map into shared memory,
+// completing on `bar`.  x * 4 bytes is a multiple of 16 (x = 0 or hd).
+__device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst_smem)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// A float in CTA `rank`'s shared memory, at the address `p` has in ours.
+__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
     return v;
-}
-
-// CTA-wide wait until *ctr >= target (bounded); thread 0 polls.
-__device__ __forceinline__ void head_barrier(uint32_t* ctr, uint32_t target) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
-        uint32_t i = 0;
-        while (ld_acquire(ctr) < target) {
-            if (++i > (1u << 24)) {
-                qdev_fail(QDEV_COMBINE_TIMEOUT);
-                break;
-            }
-            __nanosleep(20);
-        }
-    }
-    __syncthreads();
 }
 
 #ifdef QB200_ATTN_PHASES  // experiment builds only: per-CTA phase timestamps
 __device__ unsigned long long g_attn_phase[1024 * 8];
-#define ATTN_PHASE(i)                                                                         \
-    do {                                                                                      \
-        if (threadIdx.x == 0) g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + (i)] = gtimer(); \
-    } while (0)
+__device__ unsigned long long g_attn_stage[1024 * 24];
+#define ATTN_PHASE(i) (g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + (i)] = gtimer())
+#define ATTN_STAGE(i, v) \
+    if ((i) < 24) g_attn_stage[(blockIdx.y * gridDim.x + blockIdx.x) * 24 + (i)] = (v)
 #else
 #define ATTN_PHASE(i) ((void)0)
+#define ATTN_STAGE(i, v) ((void)0)
 #endif
 
-template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnArgs a) {
-    constexpr int LPP = HD / 16;                 // lanes per K row (16 floats each)
-    constexpr int PPW = 32 / LPP;                // positions per warp per K round
-    constexpr int NW = ATT_THREADS / 32;
-    constexpr int SUB = NW * PPW > ATT_SUB ? NW * PPW : ATT_SUB;  // positions per sub-chunk
-    constexpr int KR = SUB / (NW * PPW);         // K rounds per sub-chunk
-    constexpr int VL = HD / 4;                   // lanes per V row (float4 each)
-    constexpr int PL = ATT_THREADS / VL;         // V rows in flight per round
-    constexpr int VR = SUB / PL;                 // V rounds per sub-chunk
-    static_assert(KR >= 1 && VR >= 1, "sub-chunk too small");
-    extern __shared__ __align__(16) float sc[];  // [G][chunk_alloc]: scores, then e
-    __shared__ __align__(16) float qs[ATT_MAXG][HD];
+template <int HD, int G>
+__global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
+    attn_decode_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap kv_map) {
+    constexpr int NW = ATT_CWARPS, T = NW * 32;
+    constexpr uint32_t RB = HD * 4;                  // bytes of one K or V row
+    constexpr uint32_t SP = ATT_STAGE_BYTES / RB;    // rows per stage
+    constexpr int LPP = HD / 16;                     // phase 1: lanes per row, 4 float4 each
+    constexpr int PPW = 32 / LPP;                    // phase 1: rows per warp
+    static_assert(SP == NW * PPW, "one phase-1 round per stage");
+    constexpr int VQ = HD / 4;                       // phase 2: float4 columns of a V row
+    constexpr int PG = T / VQ;                       // phase 2: row groups
+    constexpr int PPG = SP / PG;                     // phase 2: rows per group per stage
+    static_assert(PPG * PG == SP, "phase-2 split");
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[ATT_MAX_SLOTS], empty[ATT_MAX_SLOTS];
     __shared__ float wred[NW][ATT_MAXG];
-    __shared__ float gmax[ATT_MAXG];
-    __shared__ __align__(16) float4 ored[PL][ATT_MAXG][VL];
-    __shared__ float lsum[ATT_MAXG];
-    if (threadIdx.x == 0) trace_mark(a.trace, 0);
-    pdl_trigger();
-    pdl_wait();
-    if (threadIdx.x == 0) trace_mark(a.trace, 1);
-    ATTN_PHASE(0);
-    const uint32_t h = blockIdx.x, c = blockIdx.y;
-    const uint32_t G = a.n_heads / a.n_kv_heads;
-    const uint32_t valid = a.step->valid, N = a.step->n_row;
-    uint32_t n_act = (valid + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK;
-    n_act = n_act < a.n_chunks ? n_act : a.n_chunks;
-    if (c >= n_act) return;
-    const uint32_t chunk = (valid + n_act - 1) / n_act;
-    const uint32_t p0 = c * chunk, p1 = min(p0 + chunk, valid);
+    __shared__ float cm[ATT_MAXG], gmx[ATT_MAXG], lsum[ATT_MAXG], linv[ATT_MAXG];
+
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* slab = a.kv_layer + (size_t)h * a.max_seq * 2 * HD;
-    uint32_t* ctr = a.sync + 4 * h;
-    const uint32_t CA = a.chunk_alloc;
+    const uint32_t CS = gridDim.x, r = blockIdx.x, h = blockIdx.y;  // cluster = one grid row
+    const uint32_t CA = a.chunk_alloc, SL = a.slots;
+    uint8_t* ring = smem;
+    float* sc = reinterpret_cast<float*>(smem + (size_t)SL * ATT_STAGE_BYTES);  // [G][CA]
+    float4* ored = reinterpret_cast<float4*>(sc + (size_t)G * CA);              // [PG][G][VQ]
+    float* opart = reinterpret_cast<float*>(ored + (size_t)PG * G * VQ);        // [G][HD]
 
-    // V of the first sub-chunk: in flight from the start, used in phase 2
-    const uint32_t vl = tid % VL, pl = tid / VL;
-    float4 vreg[VR];
-#pragma unroll
-    for (int r = 0; r < VR; ++r) {
-        const uint32_t p = p0 + pl + r * PL;
-        vreg[r] = p < p1 ? __ldg(reinterpret_cast<const float4*>(slab + (size_t)p * 2 * HD + HD) + vl)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid == 0) {
+        trace_mark(a.trace, 0);
+        ATTN_PHASE(0);
+        for (uint32_t s = 0; s < SL; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        fence_mbar_init();
     }
-    for (uint32_t i = tid; i < G * HD; i += ATT_THREADS)
-        qs[i / HD][i % HD] = a.q[(size_t)(h * G) * HD + i];
     __syncthreads();
-    ATTN_PHASE(1);
+    pdl_trigger();
+    // Step scalars come from the previous graph replay or a host copy, both
+    // complete before this grid starts.
+    const uint32_t valid = a.step->valid, N = a.step->n_row, cur = a.step->pos;
+    const uint32_t chunk = (valid + CS - 1) / CS;
+    const uint32_t p0 = min(r * chunk, valid), p1 = min(p0 + chunk, valid);
+    const int plane = (int)(a.layer * a.n_kv_heads + h);
 
-    // ---- phase 1: scores + chunk max ------------------------------------------
-    {
-        const uint32_t sub = lane % LPP, slot = lane / LPP;
-        float mx[ATT_MAXG];
-#pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g) mx[g] = -INFINITY;
-        for (uint32_t sp0 = p0; sp0 < p1; sp0 += SUB) {
-            const uint32_t sp1 = min(sp0 + SUB, p1);
-            float4 k4[KR][4];
-#pragma unroll
-            for (int r = 0; r < KR; ++r) {
-                const uint32_t p = sp0 + r * NW * PPW + warp * PPW + slot;
-                const float4* kp = reinterpret_cast<const float4*>(slab + (size_t)(p < sp1 ? p : sp0) * 2 * HD + sub * 16);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) k4[r][i] = __ldg(kp + i);
-            }
-#pragma unroll
-            for (int r = 0; r < KR; ++r) {
-                const uint32_t p = sp0 + r * NW * PPW + warp * PPW + slot;
-                const bool live = p < sp1;
-#pragma unroll
-                for (int g = 0; g < ATT_MAXG; ++g) {
-                    if (g >= (int)G) break;
-                    const float4* q4 = reinterpret_cast<const float4*>(&qs[g][sub * 16]);
-                    float d = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float4 qv = q4[i];
-                        d = __fmaf_rn(qv.x, k4[r][i].x, d);
-                        d = __fmaf_rn(qv.y, k4[r][i].y, d);
-                        d = __fmaf_rn(qv.z, k4[r][i].z, d);
-                        d = __fmaf_rn(qv.w, k4[r][i].w, d);
-                    }
-#pragma unroll
-                    for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                    const float s = __fmul_rn(d, a.scale);
-                    if (live) {
-                        if (sub == 0) sc[g * CA + (p - p0)] = s;
-                        mx[g] = fmaxf(mx[g], s);
-                    }
+    if (warp == NW) {
+        // ---- producer: K rows of the chunk, then its V rows ------------------
+        cluster_arrive();  // barrier 1 does not wait for the producer's copies
+        const uint64_t pol = l2_evict_first_policy();
+        uint32_t s = 0, ph = 0, k = 0;
+        bool waited = false, ok = true;
+        for (uint32_t pass = 0; pass < 2 && ok; ++pass) {
+            for (uint32_t sp0 = p0; sp0 < p1; sp0 += SP, ++k) {
+                if (k >= SL && !mbar_wait(&empty[s], ph ^ 1, QDEV_WAIT_EMPTY_TIMEOUT)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t n = min(SP, p1 - sp0);
+                if (!waited && sp0 + n > cur) {
+                    pdl_wait();
+                    waited = true;
+                }
+                // the whole box arrives (rows past the chunk, or past max_seq as
+                // zeros, are loaded and ignored)
+                if (lane == 0) {
+                    ATTN_STAGE(k < 6 ? k + 6 : (k < 12 ? k + 12 : 23), gtimer());
+                    mbar_arrive_expect_tx(&full[s], ATT_STAGE_BYTES);
+                    tma_load_3d(ring + (size_t)s * ATT_STAGE_BYTES, &kv_map, (int)(pass * HD), (int)sp0,
+                                plane, &full[s], pol);
+                }
+                __syncwarp();
+                if (++s == SL) {
+                    s = 0;
+                    ph ^= 1;
                 }
             }
         }
+        if (!waited) pdl_wait();  // every thread waits: the grid ends after its predecessor
+#ifdef QB200_ATTN_PHASES
+        if (lane == 0) {
+            uint32_t smid;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+            g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + 7] = smid;
+        }
+#endif
+        cluster_wait();
+        cluster_arrive();
+        cluster_wait();
+        cluster_arrive();
+        cluster_wait();
+        return;
+    }
+
+    // ---- consumers -----------------------------------------------------------------
+    pdl_wait();  // q is the previous kernel's output
+    if (tid == 0) trace_mark(a.trace, 1);
+    if (tid == 0) ATTN_PHASE(1);
+
+    uint32_t s = 0, ph = 0;
+    // phase 1: scores and chunk max
+    {
+        const uint32_t sub = lane % LPP, slot = lane / LPP, row = warp * PPW + slot;
+        // lane `sub` of a row takes float4s sub, sub + LPP, ... of q and K, so
+        // the 8 lanes of each shared-memory phase read 128 contiguous bytes;
+        // its q float4s stay in registers for the whole chunk
+        float4 qr[G][4];
 #pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g) {
-            if (g >= (int)G) break;
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                qr[g][i] = reinterpret_cast<const float4*>(a.q + (size_t)(h * G + g) * HD)[sub + i * LPP];
+        float mx[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
+        uint32_t kst = 0;
+        for (uint32_t sp0 = p0; sp0 < p1; sp0 += SP) {
+            mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
+            if (tid == 0) ATTN_STAGE(kst, gtimer());
+            ++kst;
+            const uint32_t p = sp0 + row;
+            const bool live = p < p1;
+            const float4* kr = reinterpret_cast<const float4*>(ring + (size_t)s * ATT_STAGE_BYTES + row * RB) + sub;
+            float4 k4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) k4[i] = kr[i * LPP];
+            // all heads' chains interleaved (independent accumulators), then
+            // the cross-lane sums level by level
+            float d[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) d[g] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 qv = qr[g][i];
+                    d[g] = __fmaf_rn(qv.x, k4[i].x, d[g]);
+                    d[g] = __fmaf_rn(qv.y, k4[i].y, d[g]);
+                    d[g] = __fmaf_rn(qv.z, k4[i].z, d[g]);
+                    d[g] = __fmaf_rn(qv.w, k4[i].w, d[g]);
+                }
+            }
+#pragma unroll
+            for (int o = LPP / 2; o > 0; o >>= 1)
+#pragma unroll
+                for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
+            if (live) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float sv = __fmul_rn(d[g], a.scale);
+                    if (sub == 0) sc[g * CA + (p - p0)] = sv;
+                    mx[g] = fmaxf(mx[g], sv);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == SL) {
+                s = 0;
+                ph ^= 1;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
             const float m = warp_max(mx[g]);
             if (lane == 0) wred[warp][g] = m;
         }
-        __syncthreads();
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
         if (tid < G) {
             float m = -INFINITY;
             for (int w = 0; w < NW; ++w) m = fmaxf(m, wred[w][tid]);
-            a.cmax[(size_t)(h * G + tid) * a.n_chunks + c] = m;
+            cm[tid] = m;
         }
     }
-    ATTN_PHASE(2);
-    head_barrier(ctr + 0, n_act);
-    ATTN_PHASE(3);
+    if (tid == 0) ATTN_PHASE(2);
+    cluster_arrive();
+    cluster_wait();
+    if (tid == 0) ATTN_PHASE(3);
 
-    // ---- phase 2: exponentials (upstream index rule) + partial P.V -------------
-    if (warp < G) {
+    // phase 2: global max, exponentials (upstream index rule), sums, partial P.V
+    if (tid < G) {
         float m = -INFINITY;
-        for (uint32_t i = lane; i < n_act; i += 32)
-            m = fmaxf(m, __ldcg(&a.cmax[(size_t)(h * G + warp) * a.n_chunks + i]));
-        m = warp_max(m);
-        if (lane == 0) gmax[warp] = m;
+        for (uint32_t rr = 0; rr < CS; ++rr) m = fmaxf(m, ld_dsmem(&cm[tid], rr));
+        gmx[tid] = m;
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
     const uint32_t len = p1 - p0;
     const uint32_t nvec = N < 8 ? 0u : (N / 8) * 8;
-    for (uint32_t i = tid; i < G * len; i += ATT_THREADS) {
+    for (uint32_t i = tid; i < G * len; i += T) {
         const uint32_t g = i / len, pp = i % len;
-        const float x = __fsub_rn(sc[g * CA + pp], gmax[g]);
+        const float x = __fsub_rn(sc[g * CA + pp], gmx[g]);
         sc[g * CA + pp] = (p0 + pp) < nvec ? exp_poly(x) : expf(x);
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
     if (warp < G) {
         float l = 0.0f;
         for (uint32_t pp = lane; pp < len; pp += 32) l += sc[warp * CA + pp];
@@ -223,26 +309,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
         if (lane == 0) lsum[warp] = l;
     }
     {
-        float4 o[ATT_MAXG];
+        const uint32_t dq = tid % VQ, pg = tid / VQ;
+        float4 o[G];
 #pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t sp0 = p0; sp0 < p1; sp0 += SUB) {
-            if (sp0 != p0) {  // later sub-chunks (long contexts): load now
+        for (int g = 0; g < G; ++g) o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t vst = 12;
+        for (uint32_t sp0 = p0; sp0 < p1; sp0 += SP) {
+            mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
+            if (tid == 0) ATTN_STAGE(vst, gtimer());
+            ++vst;
+            const uint8_t* stage = ring + (size_t)s * ATT_STAGE_BYTES;
 #pragma unroll
-                for (int r = 0; r < VR; ++r) {
-                    const uint32_t p = sp0 + pl + r * PL;
-                    vreg[r] = p < p1 ? __ldg(reinterpret_cast<const float4*>(slab + (size_t)p * 2 * HD + HD) + vl)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < VR; ++r) {
-                const uint32_t p = sp0 + pl + r * PL;
+            for (int j = 0; j < PPG; ++j) {
+                const uint32_t i = pg * PPG + j, p = sp0 + i;
                 if (p >= p1) break;
-                const float4 v = vreg[r];
+                const float4 v = reinterpret_cast<const float4*>(stage + i * RB)[dq];
 #pragma unroll
-                for (int g = 0; g < ATT_MAXG; ++g) {
-                    if (g >= (int)G) break;
+                for (int g = 0; g < G; ++g) {
                     const float e = sc[g * CA + (p - p0)];
                     o[g].x = __fmaf_rn(e, v.x, o[g].x);
                     o[g].y = __fmaf_rn(e, v.y, o[g].y);
@@ -250,74 +333,62 @@ __global__ void __launch_bounds__(ATT_THREADS, 2) attn_decode_kernel(const AttnA
                     o[g].w = __fmaf_rn(e, v.w, o[g].w);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == SL) {
+                s = 0;
+                ph ^= 1;
+            }
         }
 #pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g)
-            if (g < (int)G) ored[pl][g][vl] = o[g];
-        __syncthreads();
-        for (uint32_t i = tid; i < G * VL; i += ATT_THREADS) {
-            const uint32_t g = i / VL, j = i % VL;
-            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < PL; ++q) {
-                const float4 t = ored[q][g][j];
-                s.x += t.x; s.y += t.y; s.z += t.z; s.w += t.w;
+        for (int g = 0; g < G; ++g) ored[((size_t)pg * G + g) * VQ + dq] = o[g];
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        for (uint32_t i = tid; i < G * VQ; i += T) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < PG; ++q) {
+                const float4 t = ored[(size_t)q * G * VQ + i];
+                acc.x += t.x;
+                acc.y += t.y;
+                acc.z += t.z;
+                acc.w += t.w;
             }
-            reinterpret_cast<float4*>(a.opart + ((size_t)(h * G + g) * a.n_chunks + c) * HD)[j] = s;
+            reinterpret_cast<float4*>(opart)[i] = acc;  // i = g * VQ + column
         }
-        if (tid < G) a.lpart[(size_t)(h * G + tid) * a.n_chunks + c] = lsum[tid];
     }
-    ATTN_PHASE(4);
-    head_barrier(ctr + 1, n_act);
-    ATTN_PHASE(5);
+    if (tid == 0) ATTN_PHASE(4);
+    cluster_arrive();
+    cluster_wait();
+    if (tid == 0) ATTN_PHASE(5);
 
-    // ---- phase 3: this CTA's slice of the outputs --------------------------------
-    // The partials sit in L2; chunk sums are spread over lanes so every load
-    // of a warp is in flight at once.
+    // phase 3: this CTA's slice of the outputs.  Every partial of the slice
+    // is fetched at once (one DSMEM load per thread and source CTA), then
+    // summed in CTA order.
     {
-        if (warp < G) {  // softmax denominators
+        const uint32_t total = G * HD, per = (total + CS - 1) / CS;
+        const uint32_t o0 = min(r * per, total), o1 = min(o0 + per, total), n = o1 - o0;
+        float* gath = reinterpret_cast<float*>(ored);  // [CS][per] + [CS][G]; phase 2 is done with ored
+        for (uint32_t i = tid; i < CS * n; i += T) {
+            const uint32_t rr = i / n, k = i % n;
+            gath[rr * per + k] = ld_dsmem(&opart[o0 + k], rr);
+        }
+        for (uint32_t i = tid; i < CS * G; i += T) gath[CS * per + i] = ld_dsmem(&lsum[i % G], i / G);
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        if (tid < G) {
             float l = 0.0f;
-            for (uint32_t k = lane; k < n_act; k += 32)
-                l += __ldcg(&a.lpart[(size_t)(h * G + warp) * a.n_chunks + k]);
-            l = warp_sum(l);
-            if (lane == 0) gmax[warp] = __fdiv_rn(1.0f, l);  // gmax now holds 1/L
+            for (uint32_t rr = 0; rr < CS; ++rr) l += gath[CS * per + rr * G + tid];
+            linv[tid] = __fdiv_rn(1.0f, l);
         }
-        __syncthreads();
-        const uint32_t total = G * HD;
-        const uint32_t per = (total + n_act - 1) / n_act;
-        const uint32_t o0 = c * per, o1 = min(o0 + per, total);
-        if (n_act <= 8) {
-            for (uint32_t i = o0 + tid; i < o1; i += ATT_THREADS) {
-                const uint32_t g = i / HD, d = i % HD;
-                const size_t row = (size_t)(h * G + g) * a.n_chunks;
-                float s = 0.0f;
-#pragma unroll 8
-                for (uint32_t k = 0; k < n_act; ++k) s += __ldcg(&a.opart[(row + k) * HD + d]);
-                a.out[(size_t)(h * G + g) * HD + d] = __fmul_rn(s, gmax[g]);
-            }
-        } else {
-            for (uint32_t i = o0 + warp; i < o1; i += NW) {
-                const uint32_t g = i / HD, d = i % HD;
-                const size_t row = (size_t)(h * G + g) * a.n_chunks;
-                float s = 0.0f;
-                for (uint32_t k = lane; k < n_act; k += 32) s += __ldcg(&a.opart[(row + k) * HD + d]);
-                s = warp_sum(s);
-                if (lane == 0) a.out[(size_t)(h * G + g) * HD + d] = __fmul_rn(s, gmax[g]);
-            }
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        for (uint32_t k = tid; k < n; k += T) {
+            float acc = 0.0f;
+            for (uint32_t rr = 0; rr < CS; ++rr) acc += gath[rr * per + k];
+            a.out[(size_t)h * G * HD + o0 + k] = __fmul_rn(acc, linv[(o0 + k) / HD]);
         }
     }
-    // last CTA of the head resets the counters for the next launch
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(ctr + 2, 1u) == n_act - 1) {
-            ctr[0] = 0u;
-            ctr[1] = 0u;
-            ctr[2] = 0u;
-            __threadfence();
-        }
-        trace_mark(a.trace, 2);
-    }
-    ATTN_PHASE(6);
+    cluster_arrive();  // nobody leaves while its shared memory may still be read
+    cluster_wait();
+    if (tid == 0) trace_mark(a.trace, 2);
+    if (tid == 0) ATTN_PHASE(6);
 }
 
 }  // namespace qb200

@@ -99,7 +99,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtimer();
     for (uint32_t i = 0; i < Q_SPIN_LIMIT; ++i) {
+#ifdef Q_MBAR_NO_SLEEP  // experiment builds only
+        if (mbar_try_wait(bar, parity)) return true;
+#else
         if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+#endif
         if (gtimer() - t0 > Q_WAIT_NS) break;
     }
     qdev_fail(code);

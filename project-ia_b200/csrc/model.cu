@@ -15,6 +15,8 @@
 #include <cmath>
 #include <cstdlib>
 
+#include <cudaTypedefs.h>
+
 #include "runtime.cuh"
 
 namespace qb200 {
@@ -154,36 +156,28 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     // activations: carved from the device arena once; the watermark moves
     // past them so per-token work allocates nothing
     s->arena_head = 0;
-    // attention CTAs per KV head: all (n_kv x NC) must be co-resident (2 per SM)
-    s->n_chunks = std::max<uint32_t>(1, std::min<uint32_t>(
-        2u * (uint32_t)device_sms() / c.n_kv_heads,
-        (c.max_seq_len + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK));
+    if ((rc = plan_attention(s)) != Q_OK) {
+        free_model(s);
+        return rc;
+    }
     s->tok_cap = c.max_seq_len;
-    const uint32_t nh = c.n_heads;
     s->x = (float*)dev_arena_alloc(s, (size_t)D * 4);
     s->q = (float*)dev_arena_alloc(s, (size_t)D * 4);
     s->att = (float*)dev_arena_alloc(s, (size_t)D * 4);
     s->h = (float*)dev_arena_alloc(s, (size_t)H * 4);
-    s->scores = (float*)dev_arena_alloc(s, (size_t)nh * c.max_seq_len * 4);
-    s->cmax = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * 4);
-    s->opart = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * s->hd * 4);
-    s->lpart = (float*)dev_arena_alloc(s, (size_t)nh * s->n_chunks * 4);
     s->logits = (float*)dev_arena_alloc(s, (size_t)V * 4);
-    s->ticket = (uint32_t*)dev_arena_alloc(s, (size_t)c.n_kv_heads * 16);
     s->best = (unsigned long long*)dev_arena_alloc(s, 8);
     s->step = (StepParams*)dev_arena_alloc(s, sizeof(StepParams));
     s->tok_out = (uint32_t*)dev_arena_alloc(s, (size_t)s->tok_cap * 4);
     s->tok_count = (uint32_t*)dev_arena_alloc(s, 4);
     s->last_tok = (uint32_t*)dev_arena_alloc(s, 4);
-    if (!s->x || !s->q || !s->att || !s->h || !s->scores || !s->cmax || !s->opart || !s->lpart ||
-        !s->logits || !s->ticket || !s->best || !s->step || !s->tok_out || !s->tok_count ||
-        !s->last_tok) {
+    if (!s->x || !s->q || !s->att || !s->h || !s->logits || !s->best || !s->step || !s->tok_out ||
+        !s->tok_count || !s->last_tok) {
         free_model(s);
         return Q_ERR_ARENA_OOM;
     }
     s->arena_base = s->arena_head;
-    if (!cuda_ok(cudaMemsetAsync(s->ticket, 0, (size_t)c.n_kv_heads * 16, st), "init") ||
-        !cuda_ok(cudaMemsetAsync(s->best, 0, 8, st), "init") ||
+    if (!cuda_ok(cudaMemsetAsync(s->best, 0, 8, st), "init") ||
         !cuda_ok(cudaMemsetAsync(s->tok_count, 0, 4, st), "init") ||
         !cuda_ok(cudaStreamSynchronize(st), "init sync")) {
         free_model(s);
@@ -209,49 +203,150 @@ static unsigned long long* take_slot(DevState* s) {
     return p;
 }
 
-static cudaError_t enqueue_attention(DevState* s, const float* kv_layer, cudaStream_t st) {
+// The attention instantiation for (head_dim, query heads per KV head).
+template <int HD>
+static const void* attn_kernel_g(uint32_t G) {
+    switch (G) {
+        case 1: return (const void*)attn_decode_kernel<HD, 1>;
+        case 2: return (const void*)attn_decode_kernel<HD, 2>;
+        case 4: return (const void*)attn_decode_kernel<HD, 4>;
+        case 8: return (const void*)attn_decode_kernel<HD, 8>;
+        default: return nullptr;
+    }
+}
+
+static const void* attn_kernel_for(uint32_t hd, uint32_t G) {
+    switch (hd) {
+        case 32: return attn_kernel_g<32>(G);
+        case 64: return attn_kernel_g<64>(G);
+        case 128: return attn_kernel_g<128>(G);
+        default: return nullptr;
+    }
+}
+
+// Attention launch shape: the largest cluster (16, else 8, 4, 2) and the
+// deepest ring (<= 8 slots of 16 KB) with which all n_kv clusters are
+// resident at once (one wave).
+q_error_code plan_attention(DevState* s) {
+    const q_llama_config& c = s->cfg;
+    const uint32_t G = c.n_heads / c.n_kv_heads;
+    const void* kern = attn_kernel_for(s->hd, G);
+    if (!kern || G == 0 || G > (uint32_t)ATT_MAXG) return Q_ERR_INVALID_CONFIG;
+    const size_t limit = 227 * 1024 - 8 * 1024;  // dynamic shared memory beside the static part
+#ifndef QB200_ATTN_MAX_CS
+#define QB200_ATTN_MAX_CS 16
+#endif
+    for (uint32_t cs = QB200_ATTN_MAX_CS; cs >= 2; cs /= 2) {
+        if (cs > 8 &&
+            cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        const uint32_t ca = ((c.max_seq_len + cs - 1) / cs + 3) / 4 * 4;
+        for (uint32_t slots = ATT_MAX_SLOTS; slots >= 2; --slots) {
+            const size_t smem = attn_smem_bytes(G, s->hd, ca, slots);
+            if (smem > limit) continue;
+            if (!cuda_ok(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                         "attention smem attribute"))
+                return Q_ERR_INVALID_ARG;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(cs, c.n_kv_heads);
+            cfg.blockDim = dim3(ATT_THREADS);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = cs;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                continue;
+            }
+            if (n < (int)c.n_kv_heads && !(cs == 2 && slots == 2 && n >= 1)) continue;
+#ifdef QB200_ATTN_PHASES
+            fprintf(stderr, "plan_attention: cluster %u slots %u chunk_alloc %u smem %zu active clusters %d\n",
+                    cs, slots, ca, smem, n);
+#endif
+            s->att_cs = cs;
+            s->att_ca = ca;
+            s->att_slots = slots;
+            s->att_smem = smem;
+            return Q_OK;
+        }
+    }
+    set_last_error("plan_attention: no cluster shape fits", cudaErrorInvalidConfiguration);
+    return Q_ERR_INVALID_CONFIG;
+}
+
+// 3-D tensor map over the whole KV cache: x = the 2*hd floats of a position
+// (K then V), y = position, z = layer * n_kv + kv head.  Boxes of
+// ATT_STAGE_BYTES: hd floats by ATT_STAGE_BYTES / (4 hd) positions.
+static q_error_code make_kv_map(DevState* s, void* kv) {
+    static PFN_cuTensorMapEncodeTiled encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+    });
+    if (!encode) {
+        set_last_error("cuTensorMapEncodeTiled unavailable", cudaErrorNotSupported);
+        return Q_ERR_INVALID_ARG;
+    }
+    const q_llama_config& c = s->cfg;
+    const uint32_t hd = s->hd;
+    const cuuint64_t dims[3] = {2ull * hd, c.max_seq_len, (cuuint64_t)c.n_layers * c.n_kv_heads};
+    const cuuint64_t strides[2] = {2ull * hd * 4, 2ull * hd * 4 * c.max_seq_len};
+    const cuuint32_t box[3] = {hd, ATT_STAGE_BYTES / (4 * hd), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode(&s->kv_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, kv, dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_last_error("cuTensorMapEncodeTiled(kv cache)", cudaErrorInvalidValue);
+        return Q_ERR_INVALID_ARG;
+    }
+    return Q_OK;
+}
+
+static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t st) {
     AttnArgs a{};
     a.q = s->q;
-    a.kv_layer = kv_layer;
-    a.cmax = s->cmax;
-    a.opart = s->opart;
-    a.lpart = s->lpart;
-    a.sync = s->ticket;
+    a.layer = layer;
     a.trace = take_slot(s);
     a.out = s->att;
     a.step = s->step;
     a.n_heads = s->cfg.n_heads;
     a.n_kv_heads = s->cfg.n_kv_heads;
     a.max_seq = s->cfg.max_seq_len;
-    a.n_chunks = s->n_chunks;
-    a.chunk_alloc = (s->cfg.max_seq_len + s->n_chunks - 1) / s->n_chunks;
+    a.chunk_alloc = s->att_ca;
+    a.slots = s->att_slots;
     a.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
-    const size_t smem = attn_smem_bytes(s->cfg.n_heads / s->cfg.n_kv_heads, a.chunk_alloc);
-    if (smem > 64 * 1024) return cudaErrorInvalidValue;
-    for (const void* k : {(const void*)attn_decode_kernel<32>, (const void*)attn_decode_kernel<64>,
-                          (const void*)attn_decode_kernel<128>}) {
-        const cudaError_t e = ensure_smem_attr(k, 64 * 1024);
-        if (e != cudaSuccess) return e;
-    }
-    // cooperative: every CTA of the grid is resident, so the per-head
-    // barriers inside the kernel cannot wait on an unscheduled CTA; no
-    // programmatic overlap with the QKV GEMV before it for the same reason
+    // one cluster per KV head; programmatic overlap with the QKV GEMV before
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(s->cfg.n_kv_heads, s->n_chunks);
+    cfg.gridDim = dim3(s->att_cs, s->cfg.n_kv_heads);
     cfg.blockDim = dim3(ATT_THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = s->att_smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = s->att_cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
-    switch (s->hd) {
-        case 32: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<32>, a);
-        case 64: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<64>, a);
-        default: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<128>, a);
-    }
+    const void* kern = attn_kernel_for(s->hd, s->cfg.n_heads / s->cfg.n_kv_heads);
+    if (!kern) return cudaErrorInvalidValue;
+    void* params[2] = {&a, &s->kv_map};
+    return cudaLaunchKernelExC(&cfg, kern, params);
 }
 
 static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
@@ -280,7 +375,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         g.max_seq = c.max_seq_len;
         g.trace = take_slot(s);
         e = launch_gemv(s->p_qkv, g, s->gemv_scratch, st, l != 0);
-        if (e == cudaSuccess) e = enqueue_attention(s, kvl, st);
+        if (e == cudaSuccess) e = enqueue_attention(s, l, st);
         if (e != cudaSuccess) break;
         GemvArgs o{};
         o.w = s->wo[l];
@@ -396,7 +491,8 @@ q_error_code ensure_graphs(q_context* ctx, DevState* s) {
     if (s->g_trace) cudaGraphExecDestroy(s->g_trace);
     s->g_body = s->g_full = s->g_trace = nullptr;
     float* kv = (float*)ctx->kv_buffer;
-    q_error_code rc = capture(s, kv, false, &s->g_body, &s->kernels_body);
+    q_error_code rc = make_kv_map(s, kv);
+    if (rc == Q_OK) rc = capture(s, kv, false, &s->g_body, &s->kernels_body);
     if (rc == Q_OK) rc = capture(s, kv, true, &s->g_full, &s->kernels_full);
     if (rc == Q_OK) s->graph_kv = ctx->kv_buffer;
     return rc;

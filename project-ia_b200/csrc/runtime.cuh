@@ -80,6 +80,7 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 // ---- per-context device state ----------------------------------------------------
 
 struct DevState {
+    CUtensorMap kv_map;  // tiled-TMA view of this context's KV cache (attention)
     int device = 0;
     cudaStream_t stream = nullptr;
     // tier 3 device twin
@@ -88,7 +89,9 @@ struct DevState {
     // model (tier 1 in HBM)
     bool built = false;
     q_llama_config cfg{};
-    uint32_t hd = 0, kvd = 0, n_chunks = 0;
+    uint32_t hd = 0, kvd = 0;
+    uint32_t att_cs = 0, att_ca = 0, att_slots = 0;  // attention cluster size, scores per head, ring
+    size_t att_smem = 0;
     std::vector<uint8_t*> qkv, wo, gu, down;
     GemvPlan p_qkv, p_wo, p_gu, p_down;
     float* attn_norm = nullptr;  // [L][D]
@@ -102,9 +105,7 @@ struct DevState {
     std::vector<void*> weight_allocs;
     // activations (device arena, below the watermark)
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
-    float *scores = nullptr, *cmax = nullptr, *opart = nullptr, *lpart = nullptr;
     float* logits = nullptr;
-    uint32_t* ticket = nullptr;
     unsigned long long* best = nullptr;
     StepParams* step = nullptr;
     uint32_t *tok_out = nullptr, *tok_count = nullptr, *last_tok = nullptr;
@@ -127,6 +128,7 @@ void* dev_arena_alloc(DevState* s, size_t bytes);
 
 q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* model);
 q_error_code ensure_graphs(q_context* ctx, DevState* s);
+q_error_code plan_attention(DevState* s);
 q_error_code capture_trace_graph(q_context* ctx, DevState* s);
 q_error_code check_device_status(const char* where);
 void free_model(DevState* s);
