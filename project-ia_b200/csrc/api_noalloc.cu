@@ -49,11 +49,12 @@ extern "C" q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M,
     if (d_x == d_y) return Q_ERR_ALIASING;
     if (((uintptr_t)d_x & 15) || ((uintptr_t)d_packed & 15)) return Q_ERR_MISALIGNED;
     GemvPlan p;
-    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
-    if (p.scratch_bytes() > kNoAllocScratchBytes) {
+    ChainPlan cp;
+    if (!plan_single(M, K, p, cp)) return Q_ERR_INVALID_SIZE;
+    if (cp.scratch_bytes() > kNoAllocScratchBytes) {
         const std::string where = "q_b200_gemv_q4_noalloc: M=" + std::to_string(M) +
                                   " K=" + std::to_string(K) + " needs " +
-                                  std::to_string(p.scratch_bytes()) + " scratch bytes, limit " +
+                                  std::to_string(cp.scratch_bytes()) + " scratch bytes, limit " +
                                   std::to_string(kNoAllocScratchBytes);
         set_last_error(where.c_str(), cudaErrorInvalidValue);
         return Q_ERR_INVALID_SIZE;
@@ -64,7 +65,7 @@ extern "C" q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M,
     NoAllocDevice& d = g_noalloc_dev[dev];
     std::call_once(d.once, [&d] {
         d.err = cudaGetSymbolAddress(&d.scratch, g_noalloc_scratch);
-        if (d.err == cudaSuccess) d.err = ensure_smem_attr((const void*)gemv_q4_kernel, 220 * 1024);
+        if (d.err == cudaSuccess) d.err = ensure_smem_attr((const void*)gemv_q4_kernel, 227 * 1024);
     });
     Q_CUDA(d.err);
     GemvArgs a{};
@@ -72,6 +73,6 @@ extern "C" q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M,
     a.x = d_x;
     a.y = d_y;
     a.epi = EPI_STORE;
-    Q_CUDA(launch_gemv(p, a, d.scratch, (cudaStream_t)stream, false));
+    Q_CUDA(launch_single(cp, p, a, d.scratch, (cudaStream_t)stream));
     return Q_OK;
 }

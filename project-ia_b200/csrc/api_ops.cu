@@ -67,13 +67,16 @@ q_error_code q_b200_gemv_q4(const void* d_packed, uint32_t M, uint32_t K, const 
     if (d_x == d_y) return Q_ERR_ALIASING;
     if (((uintptr_t)d_x & 15) || ((uintptr_t)d_packed & 15)) return Q_ERR_MISALIGNED;
     GemvPlan p;
-    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
+    ChainPlan cp;
+    if (!plan_single(M, K, p, cp)) return Q_ERR_INVALID_SIZE;
     GemvArgs a{};
     a.w = (const uint8_t*)d_packed;
     a.x = d_x;
     a.y = d_y;
     a.epi = EPI_STORE;
-    Q_CUDA(launch_gemv(p, a, op_gemv_scratch(p), (cudaStream_t)stream, false));
+    void* scratch = op_gemv_scratch(cp.scratch_bytes());
+    if (!scratch) return Q_ERR_ALLOC_FAILED;
+    Q_CUDA(launch_single(cp, p, a, scratch, (cudaStream_t)stream));
     return Q_OK;
 }
 
@@ -90,7 +93,8 @@ q_error_code q_gemv_q4_f32_avx2(const q_tensor* w, const float* x, float* y) {
     if (w->nb[0] != (size_t)nb * sizeof(q_block_q4_0)) return Q_ERR_INVALID_ARG;
     if (!w->data) return Q_ERR_INVALID_ARG;
     GemvPlan p;
-    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
+    ChainPlan cp;
+    if (!plan_single(M, K, p, cp)) return Q_ERR_INVALID_SIZE;
     DevBuf aos, packed, dx, dy;
     q_error_code rc;
     if ((rc = to_dev(aos, w->data, (size_t)M * nb * 20)) || (rc = to_dev(dx, x, (size_t)K * 4)))
@@ -102,7 +106,9 @@ q_error_code q_gemv_q4_f32_avx2(const q_tensor* w, const float* x, float* y) {
     a.x = dx.f();
     a.y = dy.f();
     a.epi = EPI_STORE;
-    Q_CUDA(launch_gemv(p, a, op_gemv_scratch(p), op_stream(), false));
+    void* scratch = op_gemv_scratch(cp.scratch_bytes());
+    if (!scratch) return Q_ERR_ALLOC_FAILED;
+    Q_CUDA(launch_single(cp, p, a, scratch, op_stream()));
     return finish(y, dy.p, (size_t)M * 4);
 }
 
@@ -271,5 +277,11 @@ extern "C" int q_b200_dbg_attn_phases(void* host, size_t bytes) {
 }
 extern "C" int q_b200_dbg_attn_stages(void* host, size_t bytes) {
     return (int)cudaMemcpyFromSymbol(host, qb200::g_attn_stage, bytes);
+}
+#endif
+
+#ifdef QB200_CHAIN_TS
+extern "C" int q_b200_dbg_chain_ts(void* host, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(host, qb200::g_chain_ts, bytes);
 }
 #endif

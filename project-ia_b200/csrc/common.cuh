@@ -26,6 +26,7 @@ enum : uint32_t {
     QDEV_WAIT_EMPTY_TIMEOUT = 2,
     QDEV_COMBINE_TIMEOUT = 3,
     QDEV_BAD_ARG = 4,
+    QDEV_GRID_TIMEOUT = 5,
 };
 
 // The library is one translation unit (csrc/libqorus_b200.cu), so the

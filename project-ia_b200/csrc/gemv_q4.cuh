@@ -55,10 +55,15 @@ struct StepParams {  // device-resident per-step scalars (graph-replay friendly)
     uint32_t valid;  // positions 0..valid-1 are unmasked for this row
 };
 
-static constexpr int GEMV_CONSUMER_WARPS = 8;
+#ifndef QB200_GEMV_CONSUMER_WARPS
+#define QB200_GEMV_CONSUMER_WARPS 15
+#endif
+static constexpr int GEMV_CONSUMER_WARPS = QB200_GEMV_CONSUMER_WARPS;
+#define QB200_GEMV_PER_SM_BOUND (QB200_GEMV_CONSUMER_WARPS <= 8 ? 2 : 1)
 static constexpr int GEMV_THREADS = GEMV_CONSUMER_WARPS * 32 + 32;
 static constexpr uint32_t GEMV_BLOCK_BYTES = 320;  // one (slab, block) unit
-static constexpr uint32_t GEMV_BFRAG_BYTES = 96;   // x limb fragments of a block (12 lanes)
+static constexpr uint32_t GEMV_BFRAG_BYTES = 128;  // x limb fragments of a block (lanes 0..15; 12..15 zero)
+static constexpr uint32_t GEMV_FSC_BYTES = 32;     // per block: (weight, correction) for t = 0..3
 static constexpr int GEMV_XREGS = 8;               // input float4s per thread per batch
 // An RMSNorm prologue needs the whole input in one register batch.
 static constexpr uint32_t GEMV_MAX_NORM_K = GEMV_CONSUMER_WARPS * 32 * GEMV_XREGS * 4;
@@ -67,10 +72,7 @@ struct GemvArgs {
     const uint8_t* w;          // packed slab tiles
     uint32_t M, K;             // rows, cols
     uint32_t n_slabs, nb;      // slabs of 16 rows, blocks per row
-    uint32_t stage_blocks;     // blocks per ring stage
-    uint32_t n_stage;          // ring depth
     uint32_t max_parts;        // CTAs that can share one slab
-    uint32_t red_slabs;        // slab sums a CTA holds in shared memory between reductions
     const float* x;            // input vector, or the embedding table if gather
     const StepParams* step;    // per-step scalars (token, pos)
     uint32_t gather;           // non-zero: x row = x + step->token * K (embedding)
@@ -87,14 +89,29 @@ struct GemvArgs {
     const float* rope_sin;
     float* kv_layer;           // [n_kv][max_seq][2*hd] of this layer
     uint32_t hd, q_rows, kv_rows, max_seq;
+};
+
+// A chain of up to GEMV_MAX_PHASES GEMVs run by one persistent grid: phase
+// p + 1 reads what phase p wrote, so consumers pass a grid barrier between
+// phases, while the producer warps stream the next matrices' weights
+// straight through it (weights never depend on activations).
+static constexpr int GEMV_MAX_PHASES = 4;
+struct GemvChain {
+    GemvArgs ph[GEMV_MAX_PHASES];
+    uint32_t n_phases;
+    uint32_t stage_blocks;      // blocks per ring stage
+    uint32_t n_stage;           // ring depth
+    uint32_t red_slabs;         // slab sums a CTA holds in shared memory between reductions
+    uint32_t max_nb;            // largest nb of the phases (input-fragment table size)
+    uint32_t* bar;              // n_phases counters, zero between launches (n_phases > 1)
     unsigned long long* trace;  // step-trace slot (null: off)
 };
 
-// Shared memory: ring | bfrag[nb][96] | fsc[nb] float2 | red[red_slabs][8][16] | bars | misc
+// Shared memory: ring | bfrag[max_nb][128] | fsc[max_nb][4] float2 | red[red_slabs][NW][16] | bars | misc
 __host__ __device__ inline size_t gemv_smem_bytes(uint32_t nb, uint32_t stage_blocks,
                                                   uint32_t n_stage, uint32_t red_slabs) {
     return (size_t)n_stage * stage_blocks * GEMV_BLOCK_BYTES + (size_t)nb * GEMV_BFRAG_BYTES +
-           (size_t)nb * 8 + (size_t)red_slabs * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 +
+           (size_t)nb * GEMV_FSC_BYTES + (size_t)red_slabs * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 +
            64 * 4 + 128;
 }
 
@@ -138,7 +155,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uin
     if (a.epi == EPI_STORE) {
         a.y[row] = v;
     } else if (a.epi == EPI_RESID) {
-        a.y[row] = __fadd_rn(a.resid[row], v);
+        a.y[row] = __fadd_rn(__ldcg(&a.resid[row]), v);
     } else if (lane & 1) {
         return;  // pairs: the even lane writes both
     } else if (a.epi == EPI_SILU) {
@@ -168,30 +185,36 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uin
     }
 }
 
-#ifdef QB200_GEMV_PHASES  // experiment builds only: per-CTA phase timestamps
-__device__ unsigned long long g_gemv_phase[2048 * 8];
-#define GEMV_PHASE(i, v) (g_gemv_phase[blockIdx.x * 8 + (i)] = (v))
+#ifdef QB200_CHAIN_TS  // experiment builds only: per-CTA phase timestamps
+__device__ unsigned long long g_chain_ts[256 * 20];
+#define CHAIN_TS(i) \
+    if (threadIdx.x == 0) g_chain_ts[blockIdx.x * 20 + (i)] = gtimer()
 #else
-#define GEMV_PHASE(i, v) ((void)0)
+#define CHAIN_TS(i) ((void)0)
 #endif
 
-__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    constexpr uint32_t NW = GEMV_CONSUMER_WARPS, T = NW * 32;
-    const uint32_t nb = a.nb;
-    const uint32_t stage_bytes = a.stage_blocks * GEMV_BLOCK_BYTES;
-    uint8_t* ring = smem;
-    uint8_t* bfrag = ring + (size_t)a.n_stage * stage_bytes;
-    float2* fsc = reinterpret_cast<float2*>(bfrag + (size_t)nb * GEMV_BFRAG_BYTES);
-    float* red = reinterpret_cast<float*>(fsc + nb);             // [red_slabs][NW][16]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)a.red_slabs * NW * 16);
-    uint64_t* empty = full + 8;
-    float* rms_part = reinterpret_cast<float*>(empty + 8);   // [NW]
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
-    const uint32_t tid = threadIdx.x;
+// One GEMV (chain phase) for this CTA's range: input prologue, main loop over
+// the ring (slot s / parity ph carried across phases), slab reductions,
+// split-slab finish and epilogue.  Consumer threads only (T of them).
+template <uint32_t NW>
+__device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c, uint8_t* smem,
+                                           uint8_t* bfrag, float2* fsc, float* red, uint64_t* full,
+                                           uint64_t* empty, float* rms_part, uint32_t& s,
+                                           uint32_t& ph, uint32_t pidx) {
+    constexpr uint32_t T = NW * 32;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t G = gridDim.x, cta = blockIdx.x;
+    const uint32_t nb = a.nb;
+    const uint32_t stage_bytes = c.stage_blocks * GEMV_BLOCK_BYTES;
     const uint32_t NB = a.n_slabs * nb;
     const uint32_t x0 = range_begin(NB, cta, G), x1 = range_begin(NB, cta + 1, G);
+    if (x0 >= x1) return;  // (host keeps G <= NB, so never taken)
     // Only the first and last slab of the range can be shared with other
     // CTAs; resolve their owners once, here.
     const uint32_t j_first = x0 / nb, j_last = (x1 - 1) / nb;
@@ -204,47 +227,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
         own_lo[1] = cta;
         own_hi[1] = cta_of(NB, G, j_last * nb + nb - 1);
     }
-    const uint32_t n_stages = (x1 - x0 + a.stage_blocks - 1) / a.stage_blocks;
 
-    if (tid == 0) {
-        for (uint32_t s = 0; s < a.n_stage; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NW);
-        }
-        fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0) trace_mark(a.trace, 0);
-    if (tid == 0) GEMV_PHASE(0, gtimer());
-    pdl_trigger();
-
-    if (tid >= T) {
-        // ---- producer warp: stream this CTA's block range -------------------
-        if (tid == T) {
-            const uint64_t pol = l2_evict_first_policy();
-            uint32_t s = 0, ph = 0;  // ring slot and its phase parity
-            for (uint32_t k = 0, b0 = x0; k < n_stages; ++k, b0 += a.stage_blocks) {
-                if (k >= a.n_stage && !mbar_wait(&empty[s], ph ^ 1, QDEV_WAIT_EMPTY_TIMEOUT)) break;
-                const uint32_t n = min(a.stage_blocks, x1 - b0);
-                mbar_arrive_expect_tx(&full[s], n * GEMV_BLOCK_BYTES);
-                bulk_g2s(ring + (size_t)s * stage_bytes, a.w + (size_t)b0 * GEMV_BLOCK_BYTES,
-                         n * GEMV_BLOCK_BYTES, &full[s], pol);
-                if (++s == a.n_stage) {
-                    s = 0;
-                    ph ^= 1;
-                }
-            }
-            GEMV_PHASE(5, gtimer());
-        }
-        pdl_wait();  // every thread waits: the grid ends after its predecessor
-        return;
-    }
-
-    // ---- consumers: input prologue -------------------------------------------
-    pdl_wait();
-    if (tid == 0) trace_mark(a.trace, 1);
-    if (tid == 0) GEMV_PHASE(1, gtimer());
-    const uint32_t lane = tid & 31, warp = tid >> 5;
+    // ---- input prologue ------------------------------------------------------------
+    const uint32_t tsb = 4 * pidx;
+    (void)tsb;
+    CHAIN_TS(tsb + 0);
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)a.step->token * a.K;
     // All input loads are issued at once (float4, registers); a serial loop
@@ -261,7 +248,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
 #pragma unroll
         for (int r = 0; r < NR; ++r) {
             const uint32_t i = base + tid + T * r;
-            xv[r] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv[r] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             gv[r] = (g4 && i < n4) ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         if (a.x_copy && cta == 0) {
@@ -345,40 +332,39 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
                 bf[0 * 8 + w] = la;
                 bf[1 * 8 + w] = lb;
                 bf[2 * 8 + w] = lc;
+                bf[3 * 8 + w] = 0u;  // column 3 (B lanes 12..15) is zero
                 if (sub == 0) {
                     // 2^-sh = 2^(E-148): normal for E >= 22, else the
                     // subnormal 2^(E+1) * 2^-149
                     const float f = __uint_as_float(E >= 22 ? (uint32_t)(E - 21) << 23
                                                             : 1u << (E + 1));
-                    fsc[b] = make_float2(f, f * (-8.0f * (float)sx));
+                    // lane t of the D fragment: t = 0 weighs 256*D_a + D_b by
+                    // 256 f; t = 1 weighs D_c by f and adds the -8*sum(X)
+                    // correction; t = 2, 3 carry no limb and weigh 0
+                    float4* fs = reinterpret_cast<float4*>(fsc + (size_t)b * 4);
+                    fs[0] = make_float4(f * 256.0f, 0.0f, f, f * (-8.0f * (float)sx));
+                    fs[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
             }
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
-    if (tid == 0) GEMV_PHASE(2, gtimer());
-#ifdef QB200_GEMV_PHASES
-    unsigned long long ph_wait = 0, ph_flush = 0;
-#endif
+    CHAIN_TS(tsb + 1);
 
     // ---- main loop ---------------------------------------------------------------
     const uint32_t g = lane >> 2, t = lane & 3;
     // D fragment of lane (g, t): rows g and g+8, columns 2t, 2t+1.  Columns
-    // 0..2 are the limbs (a, b, c); lanes t >= 2 and column 3 see whatever
-    // B lanes 12..31 load (their rows of the limb table, reused) and are
-    // cancelled by zero weights.  t = 0: p = 256*D_a + D_b, weight 256 f;
-    // t = 1: p = D_c, weight f, plus the -8*sum(X) correction.
+    // 0..2 are the limbs (a, b, c), column 3 is zero; B lanes 16..31 repeat
+    // lanes 0..15, so columns 4..7 repeat 0..3 and lanes t >= 2 are
+    // cancelled by zero weights.  p = D[2t] * m0 + D[2t+1]: t = 0 gives
+    // 256*D_a + D_b, t = 1 gives D_c.
     const int m0 = t == 0 ? 256 : 1;
-    const int m1 = t == 0 ? 1 : 0;
-    const float wt = t == 0 ? 256.0f : (t == 1 ? 1.0f : 0.0f);
-    const float ct = t == 1 ? 1.0f : 0.0f;
     const uint32_t ring_off = 0;
-    const uint32_t bfrag_off = (uint32_t)(bfrag - smem) + (lane % 12) * 8;
-    const uint32_t fsc_off = (uint32_t)(reinterpret_cast<uint8_t*>(fsc) - smem);
+    const uint32_t bfrag_off = (uint32_t)(bfrag - smem) + (lane & 15) * 8;
+    const uint32_t fsc_off = (uint32_t)(reinterpret_cast<uint8_t*>(fsc) - smem) + t * 8;
     // One block: bytes at smem + q (weights, lane part), + sq (scales of
     // rows g, g+8), + bq (limb fragment), + fq (grid factor, correction).
-    auto block_terms = [&](uint32_t q_off, uint32_t b_off, uint32_t f_off, float& u0, float& u1,
-                           float2& sc) {
+    auto block_terms = [&](uint32_t q_off, uint32_t b_off, uint32_t f_off, float2& u, float2& sc) {
         const uint2 q = *reinterpret_cast<const uint2*>(smem + q_off);
         sc = *reinterpret_cast<const float2*>(smem + q_off + (256 + g * 8 - lane * 8));
         const uint2 bv = *reinterpret_cast<const uint2*>(smem + b_off);
@@ -390,15 +376,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
         mma_u8s8(d, q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, (q.x >> 4) & 0x0F0F0F0Fu,
                  (q.y >> 4) & 0x0F0F0F0Fu, bv.x, bv.y);
 #endif
-        const float fw = fz.x * wt;
-        const float fc = fz.y * ct;
-        u0 = __fmaf_rn((float)(d[0] * m0 + d[1] * m1), fw, fc);
-        u1 = __fmaf_rn((float)(d[2] * m0 + d[3] * m1), fw, fc);
+        const float2 pv = make_float2((float)(d[0] * m0 + d[1]), (float)(d[2] * m0 + d[3]));
+        u = __ffma2_rn(pv, make_float2(fz.x, fz.x), make_float2(fz.y, fz.y));
     };
     // Slab sums wait in red[] (per warp) and are reduced by the whole CTA
     // every red_slabs slabs and at the end: warp w finishes slabs w, w+NW, ...
     // of the batch (cross-CTA parts through the ticket, then the epilogue).
-    const uint32_t RS = a.red_slabs;
+    const uint32_t RS = c.red_slabs;
     uint32_t jl = 0, j_batch = j_first;
     auto reduce_batch = [&](uint32_t cnt) {
         asm volatile("bar.sync 1, %0;" ::"r"(T));
@@ -414,12 +398,19 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
             if (!finish) {
                 float* pp = a.part + ((size_t)j * a.max_parts) * 16;
                 if (lane < 16) pp[(cta - c_first) * 16 + lane] = v;
-                __threadfence();
+                __syncwarp();
+                // acq_rel ticket: releases this warp's parts, acquires the others'
                 uint32_t last = 0;
-                if (lane == 0) last = atomicAdd(&a.ticket[j], 1u) == c_last - c_first ? 1u : 0u;
+                if (lane == 0) {
+                    uint32_t old;
+                    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                                 : "=r"(old)
+                                 : "l"(&a.ticket[j])
+                                 : "memory");
+                    last = old == c_last - c_first ? 1u : 0u;
+                }
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
-                    __threadfence();
                     v = 0.0f;
                     if (lane < 16)
                         for (uint32_t p = 0; p <= c_last - c_first; ++p) v += __ldcg(&pp[p * 16 + lane]);
@@ -432,19 +423,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
         j_batch += cnt;
         jl = 0;
     };
-    float acc0 = 0.0f, acc1 = 0.0f;
+    float2 acc = make_float2(0.0f, 0.0f);  // rows g, g + 8
     // running ring slot / parity and current slab (no divisions per stage)
-    uint32_t s = 0, ph = 0, j = j_first, jb = j_first * nb;
-    for (uint32_t k = 0, sb0 = x0; k < n_stages; ++k, sb0 += a.stage_blocks) {
-#ifdef QB200_GEMV_PHASES
-        const unsigned long long pw0 = gtimer();
-#endif
+    uint32_t j = j_first, jb = j_first * nb;
+    for (uint32_t sb0 = x0; sb0 < x1; sb0 += c.stage_blocks) {
         mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
-#ifdef QB200_GEMV_PHASES
-        ph_wait += gtimer() - pw0;
-        if (k == 0 && tid == 0) GEMV_PHASE(3, gtimer());
-#endif
-        const uint32_t sb1 = min(sb0 + a.stage_blocks, x1);
+        const uint32_t sb1 = min(sb0 + c.stage_blocks, x1);
         for (uint32_t seg = sb0; seg < sb1;) {
             const uint32_t seg_end = min(sb1, jb + nb);
             // this warp's blocks of the segment: (b - jb) % NW == warp
@@ -455,33 +439,24 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
 #endif
             uint32_t qo = ring_off + s * stage_bytes + (b - sb0) * GEMV_BLOCK_BYTES + lane * 8;
             uint32_t bo = bfrag_off + (b - jb) * GEMV_BFRAG_BYTES;
-            uint32_t fo = fsc_off + (b - jb) * 8;
-            constexpr uint32_t QS = NW * GEMV_BLOCK_BYTES, BS = NW * GEMV_BFRAG_BYTES, FS = NW * 8;
+            uint32_t fo = fsc_off + (b - jb) * GEMV_FSC_BYTES;
+            constexpr uint32_t QS = NW * GEMV_BLOCK_BYTES, BS = NW * GEMV_BFRAG_BYTES, FS = NW * GEMV_FSC_BYTES;
             // four independent blocks per step, accumulated in block order
             for (; n >= 4; n -= 4, qo += 4 * QS, bo += 4 * BS, fo += 4 * FS) {
-                float u[4][2];
-                float2 sc[4];
+                float2 u[4], sc[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    block_terms(qo + i * QS, bo + i * BS, fo + i * FS, u[i][0], u[i][1], sc[i]);
+                for (int i = 0; i < 4; ++i) block_terms(qo + i * QS, bo + i * BS, fo + i * FS, u[i], sc[i]);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc0 = __fmaf_rn(sc[i].x, u[i][0], acc0);
-                    acc1 = __fmaf_rn(sc[i].y, u[i][1], acc1);
-                }
+                for (int i = 0; i < 4; ++i) acc = __ffma2_rn(sc[i], u[i], acc);
             }
             for (; n > 0; --n, qo += QS, bo += BS, fo += FS) {
-                float u0, u1;
-                float2 sc;
-                block_terms(qo, bo, fo, u0, u1, sc);
-                acc0 = __fmaf_rn(sc.x, u0, acc0);
-                acc1 = __fmaf_rn(sc.y, u1, acc1);
+                float2 u, sc;
+                block_terms(qo, bo, fo, u, sc);
+                acc = __ffma2_rn(sc, u, acc);
             }
             if (seg_end == jb + nb || seg_end == x1) {
-#ifdef QB200_GEMV_PHASES
-                const unsigned long long pf0 = gtimer();
-#endif
                 // slab j done for this warp: limbs (quad) -> red[jl][warp]
+                float acc0 = acc.x, acc1 = acc.y;
                 acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
                 acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
                 acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -490,14 +465,11 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
                     red[(jl * NW + warp) * 16 + g] = acc0;
                     red[(jl * NW + warp) * 16 + g + 8] = acc1;
                 }
-                acc0 = acc1 = 0.0f;
+                acc = make_float2(0.0f, 0.0f);
                 if (++jl == RS) {
                     reduce_batch(RS);
                     asm volatile("bar.sync 1, %0;" ::"r"(T));  // red[] free again
                 }
-#ifdef QB200_GEMV_PHASES
-                ph_flush += gtimer() - pf0;
-#endif
             }
             if (seg_end == jb + nb) {
                 ++j;
@@ -507,20 +479,123 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q4_kernel(const GemvArgs
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == a.n_stage) {
+        if (++s == c.n_stage) {
             s = 0;
             ph ^= 1;
         }
     }
+    CHAIN_TS(tsb + 2);
     if (jl) reduce_batch(jl);
-    if (tid == 0) trace_mark(a.trace, 2);
-#ifdef QB200_GEMV_PHASES
+    asm volatile("bar.sync 1, %0;" ::"r"(T));  // tables and red[] free for the next phase
+    CHAIN_TS(tsb + 3);
+}
+
+__global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
+    gemv_q4_kernel(const __grid_constant__ GemvChain c) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t NW = GEMV_CONSUMER_WARPS, T = NW * 32;
+    const uint32_t stage_bytes = c.stage_blocks * GEMV_BLOCK_BYTES;
+    uint8_t* ring = smem;
+    uint8_t* bfrag = ring + (size_t)c.n_stage * stage_bytes;
+    float2* fsc = reinterpret_cast<float2*>(bfrag + (size_t)c.max_nb * GEMV_BFRAG_BYTES);
+    float* red = reinterpret_cast<float*>(fsc + (size_t)c.max_nb * 4);  // [red_slabs][NW][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)c.red_slabs * NW * 16);
+    uint64_t* empty = full + 8;
+    float* rms_part = reinterpret_cast<float*>(empty + 8);      // [NW]
+    const uint32_t tid = threadIdx.x, G = gridDim.x, cta = blockIdx.x, P = c.n_phases;
+
     if (tid == 0) {
-        GEMV_PHASE(4, gtimer());
-        GEMV_PHASE(6, ph_wait);
-        GEMV_PHASE(7, ph_flush);
+        for (uint32_t s = 0; s < c.n_stage; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        fence_mbar_init();
     }
+    __syncthreads();
+    if (tid == 0) trace_mark(c.trace, 0);
+    pdl_trigger();
+
+    if (tid >= T) {
+        // ---- producer warp: every phase's block range, back to back ----------
+        if (tid == T) {
+            const uint64_t pol = l2_evict_first_policy();
+            uint32_t s = 0, ph = 0, k = 0;  // ring slot, its parity, stages issued
+            bool ok = true;
+            for (uint32_t p = 0; p < P && ok; ++p) {
+#ifdef QB200_CHAIN_NOPREFETCH  // experiment builds only: no weight prefetch across barriers
+                if (p > 0)
+                    while (ld_acquire_u32(c.bar + p - 1) < G) __nanosleep(32);
 #endif
+                const GemvArgs& a = c.ph[p];
+                const uint32_t NB = a.n_slabs * a.nb;
+                const uint32_t x0 = range_begin(NB, cta, G), x1 = range_begin(NB, cta + 1, G);
+                for (uint32_t b0 = x0; b0 < x1; b0 += c.stage_blocks, ++k) {
+                    if (k >= c.n_stage && !mbar_wait(&empty[s], ph ^ 1, QDEV_WAIT_EMPTY_TIMEOUT)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t n = min(c.stage_blocks, x1 - b0);
+#ifdef QB200_GEMV_NO_LOAD  // experiment builds only: consumers run on stale shared memory
+                    (void)pol;
+                    mbar_arrive(&full[s]);
+#else
+                    mbar_arrive_expect_tx(&full[s], n * GEMV_BLOCK_BYTES);
+                    bulk_g2s(ring + (size_t)s * stage_bytes, a.w + (size_t)b0 * GEMV_BLOCK_BYTES,
+                             n * GEMV_BLOCK_BYTES, &full[s], pol);
+#endif
+                    if (++s == c.n_stage) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+        }
+        pdl_wait();  // every thread waits: the grid ends after its predecessor
+        return;
+    }
+
+    // ---- consumers -----------------------------------------------------------------
+    pdl_wait();
+    if (tid == 0) trace_mark(c.trace, 1);
+    CHAIN_TS(16);
+    uint32_t s = 0, ph = 0;
+    for (uint32_t p = 0; p < P; ++p) {
+        if (p > 0) {
+            // grid barrier: every CTA has finished phase p - 1 (outputs written)
+            if (tid == 0) {
+                const unsigned long long t0 = gtimer();
+                while (ld_acquire_u32(c.bar + p - 1) < G) {
+                    if (gtimer() - t0 > Q_WAIT_NS) {
+                        qdev_fail(QDEV_GRID_TIMEOUT);
+                        break;
+                    }
+#ifndef QB200_CHAIN_SPIN  // experiment builds only: poll without sleeping
+                    __nanosleep(32);
+#endif
+                }
+            }
+            if (p == 2) CHAIN_TS(19);
+            asm volatile("bar.sync 1, %0;" ::"r"(T));
+        }
+        gemv_phase<NW>(c.ph[p], c, smem, bfrag, fsc, red, full, empty, rms_part, s, ph, p);
+        if (p == 1) CHAIN_TS(18);
+        if (p + 1 < P && tid == 0) {
+            // consumers passed bar.sync at the end of the phase, so this
+            // release covers every consumer thread's outputs
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c.bar + p) : "memory");
+        }
+    }
+    if (P > 1 && tid == 0) {
+        // the last CTA out clears the counters for the next launch (all CTAs
+        // are past every wait by then)
+        __threadfence();
+        if (atomicAdd(c.bar + P - 1, 1u) == G - 1) {
+            for (uint32_t i = 0; i < P; ++i) c.bar[i] = 0u;
+            __threadfence();
+        }
+    }
+    if (tid == 0) trace_mark(c.trace, 2);
+    CHAIN_TS(17);
 }
 
 // Repack upstream AoS Q4_0 blocks ([M][nb] x 20 B) into slab tiles.

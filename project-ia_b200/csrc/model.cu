@@ -42,9 +42,25 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     if (!plan_gemv(D + 2 * s->kvd, D, s->p_qkv) || !plan_gemv(D, D, s->p_wo) ||
         !plan_gemv(2 * H, D, s->p_gu) || !plan_gemv(D, H, s->p_down))
         return Q_ERR_INVALID_CONFIG;
+    // GEMV chains of a decode step: [qkv(0)], then per layer l after its
+    // attention [wo(l), gate/up(l), down(l), qkv(l+1)] ([wo, gate/up, down]
+    // for the last layer)
     {
-        const size_t sb = std::max(std::max(s->p_qkv.scratch_bytes(), s->p_wo.scratch_bytes()),
-                                   std::max(s->p_gu.scratch_bytes(), s->p_down.scratch_bytes()));
+        const GemvPlan* first[1] = {&s->p_qkv};
+        const GemvPlan* mid[4] = {&s->p_wo, &s->p_gu, &s->p_down, &s->p_qkv};
+        if (!plan_chain(first, 1, s->cp_first) || !plan_chain(mid, 4, s->cp_mid) ||
+            !plan_chain(mid, 3, s->cp_last) || !plan_chain(&mid[0], 1, s->cp_wo) ||
+            !plan_chain(&mid[1], 1, s->cp_gu) || !plan_chain(&mid[2], 1, s->cp_down))
+            return Q_ERR_INVALID_CONFIG;
+        // GEMVs per launch: 1 (separate kernels) unless QORUS_B200_CHAIN asks
+        // for the persistent chain of a layer's GEMVs
+        const char* env = std::getenv("QORUS_B200_CHAIN");
+        s->chain_phases = (env && env[0] == '1') ? 4 : 1;
+    }
+    {
+        const size_t sb = std::max(s->cp_first.scratch_bytes(),
+                                   std::max(std::max(s->cp_mid.scratch_bytes(), s->cp_last.scratch_bytes()),
+                 std::max(s->cp_wo.scratch_bytes(), std::max(s->cp_gu.scratch_bytes(), s->cp_down.scratch_bytes()))));
         void* sp = nullptr;
         q_error_code r = dalloc(s, &sp, sb);
         if (r != Q_OK) return r;
@@ -166,18 +182,20 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     s->att = (float*)dev_arena_alloc(s, (size_t)D * 4);
     s->h = (float*)dev_arena_alloc(s, (size_t)H * 4);
     s->logits = (float*)dev_arena_alloc(s, (size_t)V * 4);
+    s->chain_bar = (uint32_t*)dev_arena_alloc(s, (size_t)L * GEMV_MAX_PHASES * 4);
     s->best = (unsigned long long*)dev_arena_alloc(s, 8);
     s->step = (StepParams*)dev_arena_alloc(s, sizeof(StepParams));
     s->tok_out = (uint32_t*)dev_arena_alloc(s, (size_t)s->tok_cap * 4);
     s->tok_count = (uint32_t*)dev_arena_alloc(s, 4);
     s->last_tok = (uint32_t*)dev_arena_alloc(s, 4);
     if (!s->x || !s->q || !s->att || !s->h || !s->logits || !s->best || !s->step || !s->tok_out ||
-        !s->tok_count || !s->last_tok) {
+        !s->tok_count || !s->last_tok || !s->chain_bar) {
         free_model(s);
         return Q_ERR_ARENA_OOM;
     }
     s->arena_base = s->arena_head;
     if (!cuda_ok(cudaMemsetAsync(s->best, 0, 8, st), "init") ||
+        !cuda_ok(cudaMemsetAsync(s->chain_bar, 0, (size_t)L * GEMV_MAX_PHASES * 4, st), "init") ||
         !cuda_ok(cudaMemsetAsync(s->tok_count, 0, 4, st), "init") ||
         !cuda_ok(cudaStreamSynchronize(st), "init sync")) {
         free_model(s);
@@ -349,64 +367,72 @@ static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t s
     return cudaLaunchKernelExC(&cfg, kern, params);
 }
 
+// QKV projection of layer l (RMSNorm prologue; RoPE, KV store epilogue);
+// layer 0 gathers the embedding row and keeps a copy as the residual stream.
+static GemvArgs qkv_args(DevState* s, float* kv, uint32_t l) {
+    const q_llama_config& c = s->cfg;
+    const size_t layer_floats = (size_t)c.n_kv_heads * c.max_seq_len * 2 * s->hd;
+    GemvArgs g{};
+    g.w = s->qkv[l];
+    g.step = s->step;
+    g.gather = l == 0;
+    g.x = l == 0 ? s->embd : s->x;
+    g.x_copy = l == 0 ? s->x : nullptr;
+    g.norm_w = s->attn_norm + (size_t)l * c.dim;
+    g.eps = c.rms_norm_eps;
+    g.y = s->q;
+    g.epi = EPI_QKV;
+    g.rope_cos = s->rope_cos;
+    g.rope_sin = s->rope_sin;
+    g.kv_layer = kv + (size_t)l * layer_floats;
+    g.hd = s->hd;
+    g.q_rows = c.dim;
+    g.kv_rows = s->kvd;
+    g.max_seq = c.max_seq_len;
+    return g;
+}
+
 static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
     const q_llama_config& c = s->cfg;
     const uint32_t D = c.dim;
-    const size_t layer_floats = (size_t)c.n_kv_heads * c.max_seq_len * 2 * s->hd;
-    cudaError_t e = cudaSuccess;
+    GemvArgs first = qkv_args(s, kv, 0);
+    const GemvPlan* fm[1] = {&s->p_qkv};
+    cudaError_t e = launch_chain(s->cp_first, fm, &first, s->gemv_scratch, nullptr, take_slot(s), st, false);
     for (uint32_t l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
-        float* kvl = kv + (size_t)l * layer_floats;
-        GemvArgs g{};
-        g.w = s->qkv[l];
-        g.step = s->step;
-        g.gather = l == 0;
-        g.x = l == 0 ? s->embd : s->x;
-        g.x_copy = l == 0 ? s->x : nullptr;
-        g.norm_w = s->attn_norm + (size_t)l * D;
-        g.eps = c.rms_norm_eps;
-        g.y = s->q;
-        g.epi = EPI_QKV;
-        g.rope_cos = s->rope_cos;
-        g.rope_sin = s->rope_sin;
-        g.kv_layer = kvl;
-        g.hd = s->hd;
-        g.q_rows = D;
-        g.kv_rows = s->kvd;
-        g.max_seq = c.max_seq_len;
-        g.trace = take_slot(s);
-        e = launch_gemv(s->p_qkv, g, s->gemv_scratch, st, l != 0);
-        if (e == cudaSuccess) e = enqueue_attention(s, l, st);
+        e = enqueue_attention(s, l, st);
         if (e != cudaSuccess) break;
-        GemvArgs o{};
-        o.w = s->wo[l];
-        o.step = s->step;
-        o.x = s->att;
-        o.y = s->x;
-        o.resid = s->x;
-        o.epi = EPI_RESID;
-        o.trace = take_slot(s);
-        e = launch_gemv(s->p_wo, o, s->gemv_scratch, st, true);
-        if (e != cudaSuccess) break;
-        GemvArgs u{};
-        u.w = s->gu[l];
-        u.step = s->step;
-        u.x = s->x;
-        u.norm_w = s->ffn_norm + (size_t)l * D;
-        u.eps = c.rms_norm_eps;
-        u.y = s->h;
-        u.epi = EPI_SILU;
-        u.trace = take_slot(s);
-        e = launch_gemv(s->p_gu, u, s->gemv_scratch, st, true);
-        if (e != cudaSuccess) break;
-        GemvArgs d{};
-        d.w = s->down[l];
-        d.step = s->step;
-        d.x = s->h;
-        d.y = s->x;
-        d.resid = s->x;
-        d.epi = EPI_RESID;
-        d.trace = take_slot(s);
-        e = launch_gemv(s->p_down, d, s->gemv_scratch, st, true);
+        GemvArgs ph[4] = {};
+        ph[0].w = s->wo[l];  // attention output -> residual
+        ph[0].step = s->step;
+        ph[0].x = s->att;
+        ph[0].y = s->x;
+        ph[0].resid = s->x;
+        ph[0].epi = EPI_RESID;
+        ph[1].w = s->gu[l];  // RMSNorm -> gate/up -> SiLU(gate) * up
+        ph[1].step = s->step;
+        ph[1].x = s->x;
+        ph[1].norm_w = s->ffn_norm + (size_t)l * D;
+        ph[1].eps = c.rms_norm_eps;
+        ph[1].y = s->h;
+        ph[1].epi = EPI_SILU;
+        ph[2].w = s->down[l];  // down -> residual
+        ph[2].step = s->step;
+        ph[2].x = s->h;
+        ph[2].y = s->x;
+        ph[2].resid = s->x;
+        ph[2].epi = EPI_RESID;
+        const bool more = l + 1 < c.n_layers;
+        if (more) ph[3] = qkv_args(s, kv, l + 1);
+        const GemvPlan* mats[4] = {&s->p_wo, &s->p_gu, &s->p_down, &s->p_qkv};
+        if (s->chain_phases > 1) {
+            e = launch_chain(more ? s->cp_mid : s->cp_last, mats, ph, s->gemv_scratch,
+                             s->chain_bar + (size_t)l * GEMV_MAX_PHASES, take_slot(s), st, true);
+        } else {
+            // one GEMV per launch, chained by programmatic dependent launch
+            const ChainPlan* one[4] = {&s->cp_wo, &s->cp_gu, &s->cp_down, &s->cp_first};
+            for (uint32_t i = 0; i < (more ? 4u : 3u) && e == cudaSuccess; ++i)
+                e = launch_chain(*one[i], &mats[i], &ph[i], s->gemv_scratch, nullptr, take_slot(s), st, true);
+        }
     }
     return e;
 }

@@ -75,74 +75,139 @@ q_error_code check_device_status(const char* where) {
 }
 
 // ---- GEMV plans -----------------------------------------------------------------
-// R: largest power of two with a ~24 KB tile (4-stage ring ~96 KB, so the
-// next kernel's CTA fits beside this one under programmatic dependent
-// launch).  Threads: (nb/bpt)*c <= 256, a multiple of 32.
 
 bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     if (M == 0 || K == 0 || K % 32) return false;
     const uint32_t nb = K / 32, n_slabs = (M + 15) / 16;
-    if (n_slabs > GemvPlan::kTicketWords) return false;
-    const uint64_t NB = (uint64_t)n_slabs * nb;
-    const int sms = device_sms();
-#ifndef QB200_GEMV_STAGE_BLOCKS
-#define QB200_GEMV_STAGE_BLOCKS 64  // 20 KB stages
-#endif
-    uint32_t stage_blocks = QB200_GEMV_STAGE_BLOCKS;
-#ifndef QB200_GEMV_PER_SM
-#define QB200_GEMV_PER_SM 2
-#endif
-#ifndef QB200_GEMV_MAX_STAGES
-#define QB200_GEMV_MAX_STAGES 8
-#endif
-    uint32_t per_sm = QB200_GEMV_PER_SM, n_stage = 0;
-    // two CTAs per SM (the next kernel's CTA also fits under programmatic
-    // dependent launch) when a >= 2-stage ring fits in ~113 KB, else one
-    uint32_t red_slabs = 1;
-    for (; per_sm >= 1; --per_sm) {
-        // slabs one CTA's range touches (at most), held in shared memory
-        // between CTA-wide reductions (capped: longer ranges reduce in batches)
-        const uint64_t grid = std::min<uint64_t>(NB, (uint64_t)per_sm * sms);
-        const uint64_t range = (NB + grid - 1) / grid;
-        red_slabs = (uint32_t)std::min<uint64_t>(32, (range + nb - 1) / nb + 1);
-        const size_t fixed = gemv_smem_bytes(nb, 0, 0, red_slabs);
-        const size_t budget = per_sm == 2 ? 113 * 1024 : 220 * 1024;
-        if (budget <= fixed) continue;
-        n_stage = (uint32_t)std::min<size_t>(QB200_GEMV_MAX_STAGES,
-                                             (budget - fixed) / (stage_blocks * GEMV_BLOCK_BYTES));
-        if (n_stage >= 2) break;
-    }
-    if (per_sm < 1 || n_stage < 2) return false;
+    if (n_slabs > ChainPlan::kTicketWords) return false;
     p.M = M;
     p.K = K;
     p.n_slabs = n_slabs;
     p.nb = nb;
-    p.stage_blocks = stage_blocks;
-    p.n_stage = n_stage;
-    p.grid = (uint32_t)std::min<uint64_t>(NB, (uint64_t)per_sm * sms);
-    if (NB * p.grid >= (1ull << 32)) return false;  // the kernel's range math is 32-bit
-    const uint64_t per_cta = std::max<uint64_t>(1, NB / p.grid);
-    p.max_parts = (uint32_t)((nb + per_cta - 1) / per_cta + 2);
-    p.red_slabs = red_slabs;
-    p.smem = gemv_smem_bytes(nb, stage_blocks, n_stage, red_slabs);
-    p.packed_bytes = (size_t)NB * GEMV_BLOCK_BYTES;
+    p.packed_bytes = (size_t)p.NB() * GEMV_BLOCK_BYTES;
     return true;
 }
 
-cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, void* scratch, cudaStream_t s, bool pdl) {
-    a.M = p.M;
-    a.K = p.K;
-    a.n_slabs = p.n_slabs;
-    a.nb = p.nb;
-    a.stage_blocks = p.stage_blocks;
-    a.n_stage = p.n_stage;
-    a.max_parts = p.max_parts;
-    a.red_slabs = p.red_slabs;
-    a.ticket = reinterpret_cast<uint32_t*>(scratch);
-    a.part = reinterpret_cast<float*>(a.ticket + GemvPlan::kTicketWords);
-    const cudaError_t e = ensure_smem_attr((const void*)gemv_q4_kernel, 220 * 1024);
+// Grid: one CTA per SM (GEMV_CONSUMER_WARPS consumer warps each), fewer when a
+// phase has fewer tiles.  Every CTA takes an equal contiguous share of each
+// phase's tile stream.  Ring: the largest stage (256, 192, 128, 64 tiles)
+// that leaves room for >= 2 stages beside the input tables; as many stages
+// as fit.
+bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
+    if (n == 0 || n > (uint32_t)GEMV_MAX_PHASES) return false;
+#ifndef QB200_GEMV_PER_SM
+#define QB200_GEMV_PER_SM 1
+#endif
+#ifndef QB200_GEMV_MAX_STAGES
+#define QB200_GEMV_MAX_STAGES 8
+#endif
+    uint64_t grid = (uint64_t)QB200_GEMV_PER_SM * device_sms();
+    uint32_t max_nb = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        grid = std::min<uint64_t>(grid, mats[i]->NB());
+        max_nb = std::max(max_nb, mats[i]->nb);
+    }
+    if (grid == 0) return false;
+    cp = ChainPlan{};
+    cp.n = n;
+    cp.grid = (uint32_t)grid;
+    cp.max_nb = max_nb;
+    uint32_t red_slabs = 1;
+    for (uint32_t i = 0; i < n; ++i) {
+        const GemvPlan& m = *mats[i];
+        const uint64_t NB = m.NB();
+        if (NB * grid >= (1ull << 32)) return false;  // the kernel's range math is 32-bit
+        const uint64_t per_cta = std::max<uint64_t>(1, NB / grid);
+        cp.max_parts[i] = (uint32_t)((m.nb + per_cta - 1) / per_cta + 2);
+        cp.part_floats = std::max<size_t>(cp.part_floats, (size_t)m.n_slabs * cp.max_parts[i] * 16);
+        // slabs one CTA's range touches, held in shared memory between
+        // CTA-wide reductions (capped: longer ranges reduce in batches)
+        const uint64_t range = (NB + grid - 1) / grid;
+        red_slabs = std::max<uint32_t>(red_slabs, (uint32_t)std::min<uint64_t>(8, (range + m.nb - 1) / m.nb + 1));
+    }
+    cp.red_slabs = red_slabs;
+    const size_t budget = QB200_GEMV_PER_SM == 1 ? 220 * 1024 : 113 * 1024;
+    const size_t fixed = gemv_smem_bytes(max_nb, 0, 0, red_slabs);
+    if (fixed >= budget) return false;
+#ifdef QB200_GEMV_STAGE_BLOCKS
+    const uint32_t sizes[] = {QB200_GEMV_STAGE_BLOCKS};
+#else
+    const uint32_t sizes[] = {256, 192, 128, 64};
+#endif
+    for (uint32_t sb : sizes) {
+        const uint32_t ns = (uint32_t)std::min<size_t>(QB200_GEMV_MAX_STAGES,
+                                                       (budget - fixed) / ((size_t)sb * GEMV_BLOCK_BYTES));
+        if (ns >= 2) {
+            cp.stage_blocks = sb;
+            cp.n_stage = ns;
+            break;
+        }
+    }
+    if (cp.n_stage < 2) return false;
+    cp.smem = gemv_smem_bytes(max_nb, cp.stage_blocks, cp.n_stage, red_slabs);
+    return true;
+}
+
+cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const GemvArgs* args,
+                         void* scratch, uint32_t* bar, unsigned long long* trace, cudaStream_t s,
+                         bool pdl) {
+    GemvChain c{};
+    for (uint32_t i = 0; i < cp.n; ++i) {
+        GemvArgs a = args[i];
+        a.M = mats[i]->M;
+        a.K = mats[i]->K;
+        a.n_slabs = mats[i]->n_slabs;
+        a.nb = mats[i]->nb;
+        a.max_parts = cp.max_parts[i];
+        a.ticket = reinterpret_cast<uint32_t*>(scratch);
+        a.part = reinterpret_cast<float*>(a.ticket + ChainPlan::kTicketWords);
+        c.ph[i] = a;
+    }
+    c.n_phases = cp.n;
+    c.stage_blocks = cp.stage_blocks;
+    c.n_stage = cp.n_stage;
+    c.red_slabs = cp.red_slabs;
+    c.max_nb = cp.max_nb;
+    c.bar = bar;
+    c.trace = trace;
+    if (cp.n > 1 && !bar) return cudaErrorInvalidValue;
+    cudaError_t e = ensure_smem_attr((const void*)gemv_q4_kernel, 227 * 1024);
     if (e != cudaSuccess) return e;
-    return launch_ex(gemv_q4_kernel, dim3(p.grid), dim3(GEMV_THREADS), p.smem, s, pdl, a);
+    // Phases after the first wait on the whole grid: all CTAs must be
+    // resident at once (cooperative launch).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cp.grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = cp.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    uint32_t na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cp.n > 1) {
+        attr[na].id = cudaLaunchAttributeCooperative;
+        attr[na].val.cooperative = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaLaunchKernelEx(&cfg, gemv_q4_kernel, c);
+}
+
+bool plan_single(uint32_t M, uint32_t K, GemvPlan& p, ChainPlan& cp) {
+    if (!plan_gemv(M, K, p)) return false;
+    const GemvPlan* m[1] = {&p};
+    return plan_chain(m, 1, cp);
+}
+
+cudaError_t launch_single(const ChainPlan& cp, const GemvPlan& p, const GemvArgs& a, void* scratch,
+                          cudaStream_t s) {
+    const GemvPlan* m[1] = {&p};
+    return launch_chain(cp, m, &a, scratch, nullptr, nullptr, s, false);
 }
 
 cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,
@@ -154,23 +219,23 @@ cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave
     return cudaGetLastError();
 }
 
-void* op_gemv_scratch(const GemvPlan& p) {
+void* op_gemv_scratch(size_t bytes) {
     static std::mutex mu;
     static std::unordered_map<int, std::pair<void*, size_t>> bufs;  // device -> buffer
     std::lock_guard<std::mutex> lk(mu);
     int dev = 0;
     cudaGetDevice(&dev);
     auto& b = bufs[dev];
-    if (b.second < p.scratch_bytes()) {
+    if (b.second < bytes) {
         if (b.first) {
             cudaDeviceSynchronize();
             cudaFree(b.first);
         }
         b = {nullptr, 0};
         void* q = nullptr;
-        if (!cuda_ok(cudaMalloc(&q, p.scratch_bytes()), "cudaMalloc(gemv scratch)")) return nullptr;
-        if (!cuda_ok(cudaMemset(q, 0, p.scratch_bytes()), "memset(gemv scratch)")) return nullptr;
-        b = {q, p.scratch_bytes()};
+        if (!cuda_ok(cudaMalloc(&q, bytes), "cudaMalloc(gemv scratch)")) return nullptr;
+        if (!cuda_ok(cudaMemset(q, 0, bytes), "memset(gemv scratch)")) return nullptr;
+        b = {q, bytes};
     }
     return b.first;
 }

@@ -35,30 +35,46 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes);
         if (!::qb200::cuda_ok((call), #call)) return Q_ERR_INVALID_ARG; \
     } while (0)
 
-// ---- GEMV launch plan ---------------------------------------------------------
+// ---- GEMV launch plans -----------------------------------------------------------
 
+// One matrix: shape, slab tiling, packed size.
 struct GemvPlan {
-    uint32_t M = 0, K = 0, n_slabs = 0, nb = 0, stage_blocks = 0, n_stage = 0, max_parts = 0;
-    uint32_t grid = 0, red_slabs = 0;
-    size_t smem = 0, packed_bytes = 0;
-    // Scratch layout, shared by every plan: a fixed ticket area of
-    // kTicketWords uint32 (zero between launches: each finisher resets its
-    // ticket), then the partial sums [n_slabs][max_parts][16] fp32.
+    uint32_t M = 0, K = 0, n_slabs = 0, nb = 0;
+    size_t packed_bytes = 0;
+    uint64_t NB() const { return (uint64_t)n_slabs * nb; }
+};
+
+// A chain of 1..GEMV_MAX_PHASES matrices run by one persistent grid (one
+// CTA per SM).  Scratch layout, shared by every plan: a fixed ticket area of
+// kTicketWords uint32 (zero between launches: each finisher resets its
+// ticket), then the partial sums [n_slabs][max_parts][16] fp32 of the
+// largest phase.
+struct ChainPlan {
+    uint32_t n = 0, grid = 0, stage_blocks = 0, n_stage = 0, red_slabs = 0, max_nb = 0;
+    uint32_t max_parts[GEMV_MAX_PHASES] = {};
+    size_t smem = 0, part_floats = 0;
     static constexpr size_t kTicketWords = 16384;
-    size_t scratch_floats() const { return (size_t)n_slabs * max_parts * 16; }
-    size_t scratch_bytes() const { return kTicketWords * 4 + scratch_floats() * 4; }
+    size_t scratch_bytes() const { return kTicketWords * 4 + part_floats * 4; }
 };
 
 bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p);
-// scratch: scratch_bytes() of device memory whose ticket words (the tail,
-// n_slabs uint32 after the parts) are zero before the first launch; the
-// kernel leaves them zero again.
-cudaError_t launch_gemv(const GemvPlan& p, GemvArgs a, void* scratch, cudaStream_t s, bool pdl);
+bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp);
+// args[i]: phase i's pointers and epilogue; shapes, tiling and scratch
+// pointers are filled in here.  scratch: cp.scratch_bytes() whose ticket
+// words are zero before the first launch (kernels leave them zero); bar:
+// cp.n zeroed counters when cp.n > 1 (likewise left zero).
+cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const GemvArgs* args,
+                         void* scratch, uint32_t* bar, unsigned long long* trace, cudaStream_t s,
+                         bool pdl);
+// One GEMV on its own (a one-phase chain).
+bool plan_single(uint32_t M, uint32_t K, GemvPlan& p, ChainPlan& cp);
+cudaError_t launch_single(const ChainPlan& cp, const GemvPlan& p, const GemvArgs& a, void* scratch,
+                          cudaStream_t s);
 cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,
                     uint8_t* d_dst, cudaStream_t s);
 // Library-owned, zeroed GEMV scratch of the current device for the
 // kernel-level entry points (grown on demand; nullptr on failure).
-void* op_gemv_scratch(const GemvPlan& p);
+void* op_gemv_scratch(size_t bytes);
 
 template <typename Kern, typename Args>
 cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
@@ -94,6 +110,9 @@ struct DevState {
     size_t att_smem = 0;
     std::vector<uint8_t*> qkv, wo, gu, down;
     GemvPlan p_qkv, p_wo, p_gu, p_down;
+    ChainPlan cp_first, cp_mid, cp_last;  // [qkv], [wo, gu, down, qkv], [wo, gu, down]
+    ChainPlan cp_wo, cp_gu, cp_down;       // one GEMV per launch
+    uint32_t chain_phases = 1;
     float* attn_norm = nullptr;  // [L][D]
     float* ffn_norm = nullptr;   // [L][D]
     float* out_norm = nullptr;
@@ -107,6 +126,7 @@ struct DevState {
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
     float* logits = nullptr;
     unsigned long long* best = nullptr;
+    uint32_t* chain_bar = nullptr;  // [n_layers][GEMV_MAX_PHASES] grid-barrier counters
     StepParams* step = nullptr;
     uint32_t *tok_out = nullptr, *tok_count = nullptr, *last_tok = nullptr;
     uint32_t tok_cap = 0;
