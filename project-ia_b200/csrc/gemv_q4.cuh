@@ -304,25 +304,37 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
             // power-of-two products (sh spans -106..147); an intermediate
             // can only lose bits when the final value rounds to 0 anyway.
             const int E = m > 0.0f ? max((int)(__float_as_uint(m) >> 23), 1) : 126;
-            const int sh = 148 - E, s1 = sh >> 1, s2 = sh - s1;
-            const float p1 = __int_as_float((s1 + 127) << 23), p2 = __int_as_float((s2 + 127) << 23);
-            const int X[4] = {__float2int_rn(__fmul_rn(__fmul_rn(v.x, p1), p2)),
-                              __float2int_rn(__fmul_rn(__fmul_rn(v.y, p1), p2)),
-                              __float2int_rn(__fmul_rn(__fmul_rn(v.z, p1), p2)),
-                              __float2int_rn(__fmul_rn(__fmul_rn(v.w, p1), p2))};
-            uint32_t la = 0, lb = 0, lc = 0;
-            int sx = 0;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int c8 = (int)(int8_t)(X[q] & 0xFF);
-                const int X1 = (X[q] - c8) >> 8;
-                const int b8 = (int)(int8_t)(X1 & 0xFF);
-                const int a8 = (X1 - b8) >> 8;
-                la |= (uint32_t)(a8 & 0xFF) << (8 * q);
-                lb |= (uint32_t)(b8 & 0xFF) << (8 * q);
-                lc |= (uint32_t)(c8 & 0xFF) << (8 * q);
-                sx += X[q];
+            const int sh = 148 - E;
+            int X[4];
+            if (sh <= 127) {  // one exact product (every block but the tiniest)
+                const float p = __int_as_float((sh + 127) << 23);
+                X[0] = __float2int_rn(__fmul_rn(v.x, p));
+                X[1] = __float2int_rn(__fmul_rn(v.y, p));
+                X[2] = __float2int_rn(__fmul_rn(v.z, p));
+                X[3] = __float2int_rn(__fmul_rn(v.w, p));
+            } else {
+                const int s1 = sh >> 1, s2 = sh - s1;
+                const float p1 = __int_as_float((s1 + 127) << 23), p2 = __int_as_float((s2 + 127) << 23);
+                X[0] = __float2int_rn(__fmul_rn(__fmul_rn(v.x, p1), p2));
+                X[1] = __float2int_rn(__fmul_rn(__fmul_rn(v.y, p1), p2));
+                X[2] = __float2int_rn(__fmul_rn(__fmul_rn(v.z, p1), p2));
+                X[3] = __float2int_rn(__fmul_rn(__fmul_rn(v.w, p1), p2));
             }
+            // Balanced limbs X = 65536 a + 256 b + c, b and c in [-128, 128):
+            // c = X mod 256 (as a signed byte), b = floor((X + 128) / 256)
+            // mod 256, a = floor((X + 32896) / 65536), i.e. byte 0 of X,
+            // byte 1 of X + 0x80 and byte 2 of X + 0x8080; gathered four
+            // elements at a time with byte permutes.
+            const uint32_t Y[4] = {(uint32_t)X[0] + 0x80u, (uint32_t)X[1] + 0x80u, (uint32_t)X[2] + 0x80u,
+                                   (uint32_t)X[3] + 0x80u};
+            const uint32_t Z[4] = {Y[0] + 0x8000u, Y[1] + 0x8000u, Y[2] + 0x8000u, Y[3] + 0x8000u};
+            const uint32_t lc = __byte_perm(__byte_perm((uint32_t)X[0], (uint32_t)X[1], 0x0040),
+                                            __byte_perm((uint32_t)X[2], (uint32_t)X[3], 0x0040), 0x5410);
+            const uint32_t lb = __byte_perm(__byte_perm(Y[0], Y[1], 0x0051), __byte_perm(Y[2], Y[3], 0x0051),
+                                            0x5410);
+            const uint32_t la = __byte_perm(__byte_perm(Z[0], Z[1], 0x0062), __byte_perm(Z[2], Z[3], 0x0062),
+                                            0x5410);
+            int sx = (X[0] + X[1]) + (X[2] + X[3]);
 #pragma unroll
             for (int o = 4; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
             if (i < n4) {
