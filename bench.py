@@ -15,7 +15,9 @@ graph replayed, the argmax fed back on the device) with CUDA events on the
 library's stream.  `e2e` times K calls of the upstream entry point
 llama_forward (host token in, host logits out, so each step copies the token
 and step scalars H2D and 513 KB of logits D2H).  With --gpus N each rank
-decodes its own sequence on its own GPU (replicas; weak scaling).
+is one rank of a tensor-parallel decode of the same sequence (heads, FFN
+rows and vocab rows split over the ranks, NCCL all-reduce after wo and down;
+strong scaling: value is the sequence's tok/s).
 
 --impl reference times the upstream CPU implementation of the same path:
 the upstream AVX2 kernels (compiled from the upstream sources into
@@ -254,8 +256,18 @@ def main():
     import qorus_b200 as Q
     path, cfg = ensure_model(Q, max_seq, rank, barrier)
     t_load = time.perf_counter()
-    m = Q.Model(path)
+    tp = None
+    if world > 1:
+        # tensor parallel: rank 0 makes the NCCL id, the process group carries it
+        box = [Q.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = (rank, world, box[0])
+    m = Q.Model(path, tp=tp)
     kv = kv_image(Q, cfg)
+    if world > 1:  # this rank's KV heads: [L][n_kv/W][max_seq][K|V]
+        sh = Q.tp_shape(cfg, rank, world)
+        h0 = sh["kv0"] // (cfg.dim // cfg.n_heads)
+        kv = np.ascontiguousarray(kv.reshape(cfg.n_layers, cfg.n_kv_heads, -1)[:, h0: h0 + sh["nkv"]]).ravel()
     m.kv_write(kv)
     del kv
     t_load = time.perf_counter() - t_load
@@ -282,7 +294,7 @@ def main():
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * args.steps / (ms * 1e-3)
+    value = args.steps / (ms * 1e-3)  # one sequence (tensor parallel over all ranks)
 
     # e2e: the upstream entry point, host token in / host logits out
     tok = np.array([1], np.uint32)
@@ -297,7 +309,7 @@ def main():
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * args.steps / e2e_s
+    e2e = args.steps / e2e_s
 
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("hbm_gbs", 6650.0))
@@ -321,15 +333,18 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "f32 (q4_0 weights)", "data": "synthetic",
             "config": {"workload": "llama3-8b-q4_0 decode, batch 1, kv prefill 2048 (BASELINE configs[2])",
                        "layers": 32, "dim": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
-                       "global_batch": world, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (7 GB streamed per token)"},
             "roofline": roof,
+            # the token's bytes over all ranks' HBM (each rank streams its shard)
             "step_roofline": {"bytes_per_token": step_bytes, "achieved": round(step_gbs, 1),
-                              "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4)},
+                              "peak": round(peak * world, 1), "unit": "GB/s",
+                              "frac": round(step_gbs / (peak * world), 4)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 16,
                     "d2h_bytes_per_step": CFG8B["vocab"] * 4},

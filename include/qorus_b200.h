@@ -93,6 +93,27 @@ q_error_code q_b200_profile_step(q_llama_model* model, q_context* ctx, uint32_t 
 /* Device logits of the last forward / decode step ([vocab] fp32). */
 const float* q_b200_device_logits(q_context* ctx);
 
+/* ---- tensor parallelism over the GPUs of one node ----------------------
+ * No counterpart upstream (upstream is single-process).  One process per
+ * GPU: rank 0 calls q_b200_tp_unique_id and shares the 128 bytes with the
+ * others (any host channel); every rank then calls q_b200_tp_init with its
+ * device current, after q_init_memory and before llama_build_graph.  Rank r
+ * of W then uploads only its shard: query/KV heads [r*n/W, (r+1)*n/W) (its
+ * KV cache holds those heads only, layout [L][n_kv/W][max_seq][K|V]), FFN
+ * rows [r*H/W, ...) with the matching K-slices of wo and down, and vocab
+ * rows [r*ceil(V/W), ...) of the LM head.  NCCL all-reduces the residual
+ * after wo and down and the argmax key after the head; llama_forward
+ * returns the full gathered logits on every rank.  Requires n_heads,
+ * n_kv_heads and hidden_dim/32 divisible by W. */
+q_error_code q_b200_tp_unique_id(void* id, size_t bytes);
+q_error_code q_b200_tp_init(q_context* ctx, uint32_t rank, uint32_t world, const void* id, size_t bytes);
+
+/* Shard geometry of `rank` in `world` for cfg: out[0..12] = rank, world,
+ * local q heads, local kv heads, q width, kv width, first q row, first kv
+ * row, FFN width, first FFN row, vocab rows, first vocab row, rows per rank. */
+q_error_code q_b200_tp_shape(const q_llama_config* cfg, uint32_t rank, uint32_t world, uint32_t* out,
+                             uint32_t n);
+
 /* ---- kernel entry points on device buffers ------------------------------
  * The Q4_0 GEMV of upstream src/ops/avx2/matmul.c:98-271 on device memory.
  * Weights are first repacked from the upstream 20-byte AoS blocks into the

@@ -140,6 +140,20 @@ static size_t kv_bytes_needed(const q_llama_config& c) {
     return (size_t)c.n_layers * c.n_kv_heads * c.max_seq_len * (c.dim / c.n_heads) * 2 * 4;
 }
 
+// Tensor-parallel ranks hold their vocab rows' logits; gather every rank's
+// (ceil(V/W) rows each, in rank order) into logits_all.
+static q_error_code gather_logits(DevState* s) {
+    if (s->tp_world == 1) return Q_OK;
+    const NcclApi* n = nccl();
+    if (!n) return Q_ERR_INVALID_ARG;
+    const ncclResult_t r = n->all_gather(s->logits, s->logits_all, s->tp.v_pad, ncclFloat32, s->comm, s->stream);
+    if (r != ncclSuccess) {
+        set_last_error(n->error_string(r), cudaErrorUnknown);
+        return Q_ERR_INVALID_ARG;
+    }
+    return Q_OK;
+}
+
 static q_error_code ready(q_llama_model* model, q_context* ctx, DevState** out) {
     DevState* s = state_of(ctx, false);
     if (!s || !s->built) return Q_ERR_INVALID_ARG;
@@ -186,8 +200,9 @@ q_error_code llama_forward(q_llama_model* model, q_context* ctx, const uint32_t*
     if (rc != Q_OK) return rc;
     Q_CUDA(cudaStreamSynchronize(s->stream));  // pinned step slots may still be in use
     if ((rc = run_rows(s, tokens, seq_len, pos)) != Q_OK) return rc;
-    Q_CUDA(cudaMemcpyAsync(logits, s->logits, (size_t)model->config.vocab_size * 4,
-                           cudaMemcpyDeviceToHost, s->stream));
+    if ((rc = gather_logits(s)) != Q_OK) return rc;
+    Q_CUDA(cudaMemcpyAsync(logits, s->tp_world > 1 ? s->logits_all : s->logits,
+                           (size_t)model->config.vocab_size * 4, cudaMemcpyDeviceToHost, s->stream));
     Q_CUDA(cudaStreamSynchronize(s->stream));
     return check_device_status("llama_forward");
 }
@@ -262,7 +277,7 @@ void* q_b200_stream(q_context* ctx) {
 
 const float* q_b200_device_logits(q_context* ctx) {
     DevState* s = state_of(ctx, false);
-    return s ? s->logits : nullptr;
+    return s ? (s->tp_world > 1 ? s->logits_all : s->logits) : nullptr;
 }
 
 q_error_code q_b200_kv_write(q_context* ctx, size_t off, const void* host, size_t bytes) {

@@ -2,6 +2,7 @@
 // The kernels are header-defined and included once here, so no relocatable
 // device code (and no device link step) is needed.
 #include "runtime.cu"
+#include "tp.cu"
 #include "model.cu"
 #include "api.cu"
 #include "api_model.cu"

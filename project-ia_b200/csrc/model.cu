@@ -39,8 +39,11 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     if (!(s->hd == 32 || s->hd == 64 || s->hd == 128) || G > (uint32_t)ATT_MAXG ||
         c.n_heads % c.n_kv_heads || c.max_seq_len == 0 || D > GEMV_MAX_NORM_K || D % 4)
         return Q_ERR_INVALID_CONFIG;
-    if (!plan_gemv(D + 2 * s->kvd, D, s->p_qkv) || !plan_gemv(D, D, s->p_wo) ||
-        !plan_gemv(2 * H, D, s->p_gu) || !plan_gemv(D, H, s->p_down))
+    // this rank's shard (the whole model when tp_world == 1)
+    if (!tp_shape(c, s->tp_rank, s->tp_world, s->tp)) return Q_ERR_INVALID_CONFIG;
+    const TpShape& t = s->tp;
+    if (!plan_gemv(t.d + 2 * t.kvd, D, s->p_qkv) || !plan_gemv(D, t.d, s->p_wo) ||
+        !plan_gemv(2 * t.h, D, s->p_gu) || !plan_gemv(D, t.h, s->p_down))
         return Q_ERR_INVALID_CONFIG;
     // GEMV chains of a decode step: [qkv(0)], then per layer l after its
     // attention [wo(l), gate/up(l), down(l), qkv(l+1)] ([wo, gate/up, down]
@@ -54,8 +57,9 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
             return Q_ERR_INVALID_CONFIG;
         // GEMVs per launch: 1 (separate kernels) unless QORUS_B200_CHAIN asks
         // for the persistent chain of a layer's GEMVs
+        // (tensor-parallel ranks all-reduce between GEMVs: one per launch)
         const char* env = std::getenv("QORUS_B200_CHAIN");
-        s->chain_phases = (env && env[0] == '1') ? 4 : 1;
+        s->chain_phases = (env && env[0] == '1' && s->tp_world == 1) ? 4 : 1;
     }
     {
         const size_t sb = std::max(s->cp_first.scratch_bytes(),
@@ -69,9 +73,9 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     }
     cudaStream_t st = s->stream;
     const size_t nbD = D / 32, nbH = H / 32;
-    const size_t qkv_aos = (size_t)(D + 2 * s->kvd) * nbD * 20;
-    const size_t gu_aos = (size_t)2 * H * nbD * 20;
-    const size_t down_aos = (size_t)D * nbH * 20;
+    const size_t qkv_aos = (size_t)(t.d + 2 * t.kvd) * nbD * 20;
+    const size_t gu_aos = (size_t)2 * t.h * nbD * 20;
+    const size_t down_aos = (size_t)D * (t.h / 32) * 20;
     const size_t stage_bytes = std::max(qkv_aos, std::max(gu_aos, down_aos));
     uint8_t* stage = nullptr;
     if (!cuda_ok(cudaMalloc(&stage, stage_bytes), "cudaMalloc(stage)")) return Q_ERR_ALLOC_FAILED;
@@ -79,36 +83,50 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     auto h2d = [&](void* dst, const void* src, size_t n) {
         return cuda_ok(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, st), "upload");
     };
+    // Rows of a Q4_0 matrix are contiguous AoS blocks; a K-slice (wo, down
+    // under tensor parallelism) is gathered row by row on the host first.
+    std::vector<uint8_t> hcols;
+    auto kslice = [&](const q_tensor* w, uint32_t rows, uint32_t nb_full, uint32_t blk0,
+                      uint32_t nblk) -> const void* {
+        if (nblk == nb_full) return w->data;
+        hcols.resize((size_t)rows * nblk * 20);
+        const uint8_t* src = (const uint8_t*)w->data;
+        for (uint32_t r = 0; r < rows; ++r)
+            std::memcpy(hcols.data() + (size_t)r * nblk * 20, src + ((size_t)r * nb_full + blk0) * 20,
+                        (size_t)nblk * 20);
+        return hcols.data();
+    };
+    const size_t rowD = (size_t)nbD * 20;  // bytes of one row with K = D
     void* p = nullptr;
     for (uint32_t l = 0; l < L && rc == Q_OK; ++l) {
         const q_llama_layer& ly = model->layers[l];
         if ((rc = dalloc(s, &p, s->p_qkv.packed_bytes))) break;
         s->qkv.push_back((uint8_t*)p);
-        if (!h2d(stage, ly.wq->data, (size_t)D * nbD * 20) ||
-            !h2d(stage + (size_t)D * nbD * 20, ly.wk->data, (size_t)s->kvd * nbD * 20) ||
-            !h2d(stage + (size_t)(D + s->kvd) * nbD * 20, ly.wv->data, (size_t)s->kvd * nbD * 20) ||
+        if (!h2d(stage, (const uint8_t*)ly.wq->data + t.q0 * rowD, t.d * rowD) ||
+            !h2d(stage + t.d * rowD, (const uint8_t*)ly.wk->data + t.kv0 * rowD, t.kvd * rowD) ||
+            !h2d(stage + (t.d + t.kvd) * rowD, (const uint8_t*)ly.wv->data + t.kv0 * rowD, t.kvd * rowD) ||
             !cuda_ok(pack_q4(stage, s->p_qkv, 0, s->qkv.back(), st), "pack qkv")) {
             rc = Q_ERR_INVALID_ARG;
             break;
         }
         if ((rc = dalloc(s, &p, s->p_wo.packed_bytes))) break;
         s->wo.push_back((uint8_t*)p);
-        if (!h2d(stage, ly.wo->data, (size_t)D * nbD * 20) ||
+        if (!h2d(stage, kslice(ly.wo, D, nbD, t.q0 / 32, t.d / 32), (size_t)D * (t.d / 32) * 20) ||
             !cuda_ok(pack_q4(stage, s->p_wo, 0, s->wo.back(), st), "pack wo")) {
             rc = Q_ERR_INVALID_ARG;
             break;
         }
         if ((rc = dalloc(s, &p, s->p_gu.packed_bytes))) break;
         s->gu.push_back((uint8_t*)p);
-        if (!h2d(stage, ly.w_gate->data, (size_t)H * nbD * 20) ||
-            !h2d(stage + (size_t)H * nbD * 20, ly.w_up->data, (size_t)H * nbD * 20) ||
-            !cuda_ok(pack_q4(stage, s->p_gu, H, s->gu.back(), st), "pack gate/up")) {
+        if (!h2d(stage, (const uint8_t*)ly.w_gate->data + t.h0 * rowD, t.h * rowD) ||
+            !h2d(stage + t.h * rowD, (const uint8_t*)ly.w_up->data + t.h0 * rowD, t.h * rowD) ||
+            !cuda_ok(pack_q4(stage, s->p_gu, t.h, s->gu.back(), st), "pack gate/up")) {
             rc = Q_ERR_INVALID_ARG;
             break;
         }
         if ((rc = dalloc(s, &p, s->p_down.packed_bytes))) break;
         s->down.push_back((uint8_t*)p);
-        if (!h2d(stage, ly.w_down->data, down_aos) ||
+        if (!h2d(stage, kslice(ly.w_down, D, nbH, t.h0 / 32, t.h / 32), down_aos) ||
             !cuda_ok(pack_q4(stage, s->p_down, 0, s->down.back(), st), "pack down")) {
             rc = Q_ERR_INVALID_ARG;
             break;
@@ -134,10 +152,13 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
         s->embd = (float*)p;
         if (!h2d(p, model->token_embd->data, (size_t)V * D * 4)) rc = Q_ERR_INVALID_ARG;
     }
-    if (rc == Q_OK && !(rc = dalloc(s, &p, (size_t)V * D * 4))) {
+    if (rc == Q_OK && !(rc = dalloc(s, &p, (size_t)t.v * D * 4))) {  // this rank's vocab rows
         s->out_w = (float*)p;
-        if (!h2d(p, model->output->data, (size_t)V * D * 4)) rc = Q_ERR_INVALID_ARG;
+        if (!h2d(p, (const float*)model->output->data + (size_t)t.v0 * D, (size_t)t.v * D * 4))
+            rc = Q_ERR_INVALID_ARG;
     }
+    if (rc == Q_OK && s->tp_world > 1 && !(rc = dalloc(s, &p, (size_t)s->tp_world * t.v_pad * 4)))
+        s->logits_all = (float*)p;
     // RoPE tables, host-built like upstream model.c:625-665
     const size_t tab = (size_t)c.max_seq_len * s->hd;
     std::vector<float> ct(tab), stb(tab);
@@ -268,7 +289,7 @@ q_error_code plan_attention(DevState* s) {
                          "attention smem attribute"))
                 return Q_ERR_INVALID_ARG;
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(cs, c.n_kv_heads);
+            cfg.gridDim = dim3(cs, s->tp.nkv);
             cfg.blockDim = dim3(ATT_THREADS);
             cfg.dynamicSmemBytes = smem;
             cudaLaunchAttribute attr[1];
@@ -283,7 +304,7 @@ q_error_code plan_attention(DevState* s) {
                 cudaGetLastError();
                 continue;
             }
-            if (n < (int)c.n_kv_heads && !(cs == 2 && slots == 2 && n >= 1)) continue;
+            if (n < (int)s->tp.nkv && !(cs == 2 && slots == 2 && n >= 1)) continue;
 #ifdef QB200_ATTN_PHASES
             fprintf(stderr, "plan_attention: cluster %u slots %u chunk_alloc %u smem %zu active clusters %d\n",
                     cs, slots, ca, smem, n);
@@ -318,7 +339,8 @@ static q_error_code make_kv_map(DevState* s, void* kv) {
     }
     const q_llama_config& c = s->cfg;
     const uint32_t hd = s->hd;
-    const cuuint64_t dims[3] = {2ull * hd, c.max_seq_len, (cuuint64_t)c.n_layers * c.n_kv_heads};
+    // (a tensor-parallel rank's cache holds its own KV heads only)
+    const cuuint64_t dims[3] = {2ull * hd, c.max_seq_len, (cuuint64_t)c.n_layers * s->tp.nkv};
     const cuuint64_t strides[2] = {2ull * hd * 4, 2ull * hd * 4 * c.max_seq_len};
     const cuuint32_t box[3] = {hd, ATT_STAGE_BYTES / (4 * hd), 1};
     const cuuint32_t estr[3] = {1, 1, 1};
@@ -339,15 +361,15 @@ static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t s
     a.trace = take_slot(s);
     a.out = s->att;
     a.step = s->step;
-    a.n_heads = s->cfg.n_heads;
-    a.n_kv_heads = s->cfg.n_kv_heads;
+    a.n_heads = s->tp.nh;
+    a.n_kv_heads = s->tp.nkv;
     a.max_seq = s->cfg.max_seq_len;
     a.chunk_alloc = s->att_ca;
     a.slots = s->att_slots;
     a.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
     // one cluster per KV head; programmatic overlap with the QKV GEMV before
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(s->att_cs, s->cfg.n_kv_heads);
+    cfg.gridDim = dim3(s->att_cs, s->tp.nkv);
     cfg.blockDim = dim3(ATT_THREADS);
     cfg.dynamicSmemBytes = s->att_smem;
     cfg.stream = st;
@@ -371,7 +393,7 @@ static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t s
 // layer 0 gathers the embedding row and keeps a copy as the residual stream.
 static GemvArgs qkv_args(DevState* s, float* kv, uint32_t l) {
     const q_llama_config& c = s->cfg;
-    const size_t layer_floats = (size_t)c.n_kv_heads * c.max_seq_len * 2 * s->hd;
+    const size_t layer_floats = (size_t)s->tp.nkv * c.max_seq_len * 2 * s->hd;
     GemvArgs g{};
     g.w = s->qkv[l];
     g.step = s->step;
@@ -386,10 +408,32 @@ static GemvArgs qkv_args(DevState* s, float* kv, uint32_t l) {
     g.rope_sin = s->rope_sin;
     g.kv_layer = kv + (size_t)l * layer_floats;
     g.hd = s->hd;
-    g.q_rows = c.dim;
-    g.kv_rows = s->kvd;
+    g.q_rows = s->tp.d;
+    g.kv_rows = s->tp.kvd;
     g.max_seq = c.max_seq_len;
     return g;
+}
+
+// The residual update of wo / down: y = x + W v, except on tensor-parallel
+// ranks other than 0, which store their partial W v alone (the all-reduce
+// that follows adds the partials and rank 0's x).
+static int residual_epi(const DevState* s) {
+    return s->tp_world > 1 && s->tp_rank != 0 ? EPI_STORE : EPI_RESID;
+}
+
+static cudaError_t nccl_status(ncclResult_t r) {
+    if (r == ncclSuccess) return cudaSuccess;
+    const NcclApi* n = nccl();
+    set_last_error(n ? n->error_string(r) : "nccl", cudaErrorUnknown);
+    return cudaErrorUnknown;
+}
+
+// In-place sum of `count` floats over the tensor-parallel ranks (no-op alone).
+static cudaError_t allreduce_sum(DevState* s, float* buf, size_t count, cudaStream_t st) {
+    if (s->tp_world == 1) return cudaSuccess;
+    const NcclApi* n = nccl();
+    if (!n) return cudaErrorUnknown;
+    return nccl_status(n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, s->comm, st));
 }
 
 static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
@@ -407,7 +451,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         ph[0].x = s->att;
         ph[0].y = s->x;
         ph[0].resid = s->x;
-        ph[0].epi = EPI_RESID;
+        ph[0].epi = residual_epi(s);
         ph[1].w = s->gu[l];  // RMSNorm -> gate/up -> SiLU(gate) * up
         ph[1].step = s->step;
         ph[1].x = s->x;
@@ -420,7 +464,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         ph[2].x = s->h;
         ph[2].y = s->x;
         ph[2].resid = s->x;
-        ph[2].epi = EPI_RESID;
+        ph[2].epi = residual_epi(s);
         const bool more = l + 1 < c.n_layers;
         if (more) ph[3] = qkv_args(s, kv, l + 1);
         const GemvPlan* mats[4] = {&s->p_wo, &s->p_gu, &s->p_down, &s->p_qkv};
@@ -430,8 +474,11 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         } else {
             // one GEMV per launch, chained by programmatic dependent launch
             const ChainPlan* one[4] = {&s->cp_wo, &s->cp_gu, &s->cp_down, &s->cp_first};
-            for (uint32_t i = 0; i < (more ? 4u : 3u) && e == cudaSuccess; ++i)
+            for (uint32_t i = 0; i < (more ? 4u : 3u) && e == cudaSuccess; ++i) {
                 e = launch_chain(*one[i], &mats[i], &ph[i], s->gemv_scratch, nullptr, take_slot(s), st, true);
+                // wo and down hold partial residual updates on a tensor-parallel rank
+                if (e == cudaSuccess && (i == 0 || i == 2)) e = allreduce_sum(s, s->x, c.dim, st);
+            }
         }
     }
     return e;
@@ -443,9 +490,9 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     h.x = s->x;
     h.norm_w = s->out_norm;
     h.eps = s->cfg.rms_norm_eps;
-    h.rows = s->cfg.vocab_size;
+    h.rows = s->tp.v;
     h.K = s->cfg.dim;
-    h.row_base = 0;
+    h.row_base = s->tp.v0;
     h.logits = s->logits;
     h.best = s->best;
     h.trace = take_slot(s);
@@ -454,7 +501,7 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
         if (e != cudaSuccess) return e;
     }
     const uint32_t grid = std::max<uint32_t>(
-        1, std::min<uint32_t>(2 * device_sms(), (s->cfg.vocab_size + 15) / 16));
+        1, std::min<uint32_t>(2 * device_sms(), (s->tp.v + 15) / 16));
     // The grid-stride row loop gives every CTA the same work, so CTAs must
     // spread evenly over the SMs.  Launched early under programmatic
     // dependent launch, the scheduler would otherwise stack many CTAs on the
@@ -463,6 +510,12 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     const size_t smem = std::max<size_t>((size_t)s->cfg.dim * 4, 96 * 1024);
     cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), smem, st, true, h);
     if (e != cudaSuccess) return e;
+    if (s->tp_world > 1) {  // the argmax key over every rank's vocab rows
+        const NcclApi* n = nccl();
+        if (!n) return cudaErrorUnknown;
+        e = nccl_status(n->all_reduce(s->best, s->best, 1, ncclUint64, ncclMax, s->comm, st));
+        if (e != cudaSuccess) return e;
+    }
     AdvanceArgs a{};
     a.step = s->step;
     a.best = s->best;

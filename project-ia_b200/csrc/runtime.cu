@@ -271,6 +271,10 @@ void state_erase(const q_context* ctx) {
     }
     cudaStreamSynchronize(s->stream);
     free_model(s);
+    if (s->comm) {
+        if (const NcclApi* n = nccl()) n->comm_destroy(s->comm);
+        s->comm = nullptr;
+    }
     if (s->arena) cudaFree(s->arena);
     if (s->h_step) cudaFreeHost(s->h_step);
     cudaStreamDestroy(s->stream);

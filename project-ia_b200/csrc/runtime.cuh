@@ -15,6 +15,7 @@
 #include "head.cuh"
 #include "ops.cuh"
 #include "qorus_b200.h"
+#include "tp.cuh"
 
 namespace qb200 {
 
@@ -98,6 +99,11 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
 struct DevState {
     CUtensorMap kv_map;  // tiled-TMA view of this context's KV cache (attention)
     int device = 0;
+    // tensor parallelism (q_b200_tp_init before llama_build_graph)
+    uint32_t tp_rank = 0, tp_world = 1;
+    ncclComm_t comm = nullptr;
+    TpShape tp{};
+    float* logits_all = nullptr;  // [world * v_pad] gathered logits (world > 1)
     cudaStream_t stream = nullptr;
     // tier 3 device twin
     uint8_t* arena = nullptr;

@@ -136,6 +136,9 @@ _SIGS = {
     "q_b200_gemv_q4": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_gemv_q4_noalloc": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_gemv_f32": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
+    "q_b200_tp_unique_id": (_i, [_vp, _sz]),
+    "q_b200_tp_init": (_i, [_vp, _u32, _u32, _vp, _sz]),
+    "q_b200_tp_shape": (_i, [_vp, _u32, _u32, _vp, _u32]),
     "q_b200_kernel_launches": (_u64, []),
     "q_b200_last_error": (C.c_char_p, []),
 }
@@ -189,6 +192,21 @@ TINY = dict(vocab=259, dim=256, hidden=768, layers=2, heads=8, kv_heads=2, max_s
 LLAMA3_8B = dict(vocab=128256, dim=4096, hidden=14336, layers=32, heads=32, kv_heads=8)
 
 
+def tp_unique_id() -> bytes:
+    """128-byte NCCL id for q_b200_tp_init (made once, on rank 0)."""
+    buf = C.create_string_buffer(128)
+    check(lib.q_b200_tp_unique_id(buf, 128), "q_b200_tp_unique_id")
+    return buf.raw
+
+
+def tp_shape(cfg: q_llama_config, rank: int, world: int) -> dict:
+    """Shard geometry of a tensor-parallel rank (q_b200_tp_shape)."""
+    out = (C.c_uint32 * 13)()
+    check(lib.q_b200_tp_shape(C.byref(cfg), rank, world, out, 13), "q_b200_tp_shape")
+    keys = ("rank", "world", "nh", "nkv", "d", "kvd", "q0", "kv0", "h", "h0", "v", "v0", "v_pad")
+    return dict(zip(keys, list(out)))
+
+
 def write_model(path: str, cfg: q_llama_config, seed: int = 0, threads: int = 0) -> int:
     check(lib.q_b200_write_model_file(str(path).encode(), C.byref(cfg), seed, threads),
           "q_b200_write_model_file")
@@ -203,10 +221,16 @@ def kv_bytes(cfg: q_llama_config) -> int:
 class Model:
     """A model loaded through the upstream API: init -> kv -> arena -> build."""
 
-    def __init__(self, path: str, arena_bytes: int | None = None):
+    def __init__(self, path: str, arena_bytes: int | None = None, tp: tuple | None = None):
+        """tp = (rank, world, nccl_id bytes) for a tensor-parallel rank (one process per GPU,
+        its device current); the id comes from tp_unique_id() on rank 0."""
         self.ctx = q_context()
         self.model = q_llama_model()
         check(lib.q_init_memory(C.byref(self.ctx), str(path).encode()), "q_init_memory")
+        if tp is not None:
+            rank, world, uid = tp
+            buf = C.create_string_buffer(bytes(uid), len(uid))
+            check(lib.q_b200_tp_init(C.byref(self.ctx), rank, world, buf, len(uid)), "q_b200_tp_init")
         hdr = np.frombuffer((C.c_uint32 * 16).from_address(self.ctx.header), np.uint32)
         cfg = config(int(hdr[2]), int(hdr[3]), int(hdr[4]), int(hdr[5]), int(hdr[6]),
                      int(hdr[7]), int(hdr[8]))

@@ -1,0 +1,93 @@
+"""Tensor parallelism on 2 GPUs (skipped on single-GPU machines): two ranks,
+one process per GPU, each holding its shard; NCCL all-reduces inside the
+decode graph.  The gathered logits and greedy tokens must match the upstream
+kernels' golden outputs for the tiny config (logits max-abs <= 1e-2,
+identical tokens), and each rank's KV cache (its own KV heads) must match
+the CPU oracle's rows for those heads."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle as O
+import qorus_b200 as Q
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, path, prompt, out):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)  # host channel for the NCCL id
+    try:
+        box = [Q.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        m = Q.Model(path, tp=(rank, world, box[0]))
+        first = m.forward(prompt, 0).copy()
+        toks = [int(np.argmax(first))]
+        for i in range(31):
+            lg = m.forward(np.array([toks[-1]], np.uint32), len(prompt) + i)
+            toks.append(int(np.argmax(lg)))
+        last = lg.copy()
+        kv = np.zeros(m.kv_size // 4, np.float32)
+        m.kv_read(kv)
+        dev_loop = m.decode_loop(toks[-1], len(prompt) + 31, 8).tolist()
+        shape = Q.tp_shape(m.cfg, rank, world)
+        out.put((rank, first, last, toks, kv, shape, dev_loop))
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    prompt = golden["tiny_prompt"]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, tiny_path, prompt, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r = q.get(timeout=300)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # the oracle's cache after the same 64 + 31 positions
+    orc = O.OracleModel(tiny_path)
+    orc.forward(prompt, 0)
+    for i, t in enumerate(golden["tiny_tokens"][:31]):
+        orc.forward(np.array([t], np.uint32), len(prompt) + i)
+    cfg = Q.config(**Q.TINY)
+    hd = cfg.dim // cfg.n_heads
+    ref_kv = orc.kv.reshape(cfg.n_layers, cfg.n_kv_heads, cfg.max_seq_len, 2 * hd)
+    valid = len(prompt) + 31
+    for rank in range(2):
+        _, first, last, toks, kv, sh, loop = res[rank]
+        assert np.abs(first - golden["tiny_prefill_logits"]).max() <= LOGIT_TOL
+        assert toks == list(golden["tiny_tokens"])
+        assert np.abs(last - golden["tiny_last_logits"]).max() <= LOGIT_TOL
+        h0 = sh["kv0"] // hd
+        mine = kv[: cfg.n_layers * sh["nkv"] * cfg.max_seq_len * 2 * hd].reshape(
+            cfg.n_layers, sh["nkv"], cfg.max_seq_len, 2 * hd)
+        ref = ref_kv[:, h0: h0 + sh["nkv"], :valid].astype(np.float64)
+        err = np.abs(mine[:, :, :valid] - ref)
+        assert (err <= np.maximum(1.5e-4, 1e-4 * np.abs(ref))).all(), f"kv worst {err.max():.3e}"
+    assert res[0][6] == res[1][6]  # device-fed decode agrees across ranks
+    orc.close()
