@@ -262,7 +262,12 @@ def main():
         box = [Q.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         tp = (rank, world, box[0])
-    m = Q.Model(path, tp=tp)
+
+    def gather(b):  # CUDA IPC handles of the peer-memory all-reduce buffers
+        allb = [None] * world
+        dist.all_gather_object(allb, b)
+        return allb
+    m = Q.Model(path, tp=tp, tp_gather=gather if world > 1 else None)
     kv = kv_image(Q, cfg)
     if world > 1:  # this rank's KV heads: [L][n_kv/W][max_seq][K|V]
         sh = Q.tp_shape(cfg, rank, world)

@@ -108,6 +108,14 @@ const float* q_b200_device_logits(q_context* ctx);
 q_error_code q_b200_tp_unique_id(void* id, size_t bytes);
 q_error_code q_b200_tp_init(q_context* ctx, uint32_t rank, uint32_t world, const void* id, size_t bytes);
 
+/* Optional, after q_b200_tp_init and before llama_build_graph: the decode
+ * graph's all-reduces then run as one-shot exchanges over NVLink peer
+ * memory instead of NCCL.  Each rank gets the CUDA IPC handle (64 bytes) of
+ * its exchange buffer, the handles are shared in rank order over any host
+ * channel, and each rank maps the others' buffers. */
+q_error_code q_b200_tp_ipc_handle(q_context* ctx, void* handle, size_t bytes);
+q_error_code q_b200_tp_ipc_open(q_context* ctx, const void* handles, size_t bytes);
+
 /* Shard geometry of `rank` in `world` for cfg: out[0..12] = rank, world,
  * local q heads, local kv heads, q width, kv width, first q row, first kv
  * row, FFN width, first FFN row, vocab rows, first vocab row, rows per rank. */

@@ -144,6 +144,10 @@ static size_t kv_bytes_needed(const q_llama_config& c) {
 // (ceil(V/W) rows each, in rank order) into logits_all.
 static q_error_code gather_logits(DevState* s) {
     if (s->tp_world == 1) return Q_OK;
+    if (s->peers_ready) {
+        Q_CUDA(tp_allreduce(s, s->logits, s->tp.v_pad, TP_GATHER_F32, s->stream, s->logits_all));
+        return Q_OK;
+    }
     const NcclApi* n = nccl();
     if (!n) return Q_ERR_INVALID_ARG;
     const ncclResult_t r = n->all_gather(s->logits, s->logits_all, s->tp.v_pad, ncclFloat32, s->comm, s->stream);

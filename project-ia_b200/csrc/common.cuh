@@ -27,6 +27,7 @@ enum : uint32_t {
     QDEV_COMBINE_TIMEOUT = 3,
     QDEV_BAD_ARG = 4,
     QDEV_GRID_TIMEOUT = 5,
+    QDEV_PEER_TIMEOUT = 6,
 };
 
 // The library is one translation unit (csrc/libqorus_b200.cu), so the

@@ -431,6 +431,10 @@ static cudaError_t nccl_status(ncclResult_t r) {
 // In-place sum of `count` floats over the tensor-parallel ranks (no-op alone).
 static cudaError_t allreduce_sum(DevState* s, float* buf, size_t count, cudaStream_t st) {
     if (s->tp_world == 1) return cudaSuccess;
+#ifdef QB200_TP_NO_ALLREDUCE  // experiment builds only: timing without the collective (wrong results)
+    return cudaSuccess;
+#endif
+    if (s->peers_ready) return tp_allreduce(s, buf, (uint32_t)count, TP_SUM_F32, st);
     const NcclApi* n = nccl();
     if (!n) return cudaErrorUnknown;
     return nccl_status(n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, s->comm, st));
@@ -510,7 +514,10 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     const size_t smem = std::max<size_t>((size_t)s->cfg.dim * 4, 96 * 1024);
     cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), smem, st, true, h);
     if (e != cudaSuccess) return e;
-    if (s->tp_world > 1) {  // the argmax key over every rank's vocab rows
+    if (s->tp_world > 1 && s->peers_ready) {  // the argmax key over every rank's vocab rows
+        e = tp_allreduce(s, s->best, 1, TP_MAX_U64, st);
+        if (e != cudaSuccess) return e;
+    } else if (s->tp_world > 1) {
         const NcclApi* n = nccl();
         if (!n) return cudaErrorUnknown;
         e = nccl_status(n->all_reduce(s->best, s->best, 1, ncclUint64, ncclMax, s->comm, st));

@@ -104,6 +104,10 @@ struct DevState {
     ncclComm_t comm = nullptr;
     TpShape tp{};
     float* logits_all = nullptr;  // [world * v_pad] gathered logits (world > 1)
+    void* peer_buf = nullptr;     // this rank's one-shot all-reduce buffer (IPC-shared)
+    TpPeers peers{};
+    uint32_t peer_slice = 0;      // floats per slot of the exchange buffer
+    bool peers_ready = false;
     cudaStream_t stream = nullptr;
     // tier 3 device twin
     uint8_t* arena = nullptr;
@@ -157,6 +161,8 @@ q_error_code ensure_graphs(q_context* ctx, DevState* s);
 q_error_code plan_attention(DevState* s);
 q_error_code capture_trace_graph(q_context* ctx, DevState* s);
 q_error_code check_device_status(const char* where);
+cudaError_t tp_allreduce(DevState* s, void* data, uint32_t n, int op, cudaStream_t st,
+                         float* out = nullptr);
 void free_model(DevState* s);
 
 }  // namespace qb200

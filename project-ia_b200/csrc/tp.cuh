@@ -47,4 +47,34 @@ struct NcclApi {
 // The process's NCCL (nullptr, with the last error set, when unavailable).
 const NcclApi* nccl();
 
+// ---- one-shot all-reduce over peer memory ------------------------------------
+// Every rank owns a buffer (shared with the others through CUDA IPC):
+//   recv[2][W][slice] fp32 | flags[2][W] u32 | seq u32
+// (slice = max(dim, ceil(vocab / W)) floats, a multiple of 4).
+// An all-reduce of sequence number q (counted on each rank; every rank runs
+// the same sequence) uses parity q & 1: each rank stores its n values into
+// recv[q&1][rank] of every rank over NVLink (plain stores, no TMA), fences,
+// and sets flags[q&1][rank] = q on every rank (release, system scope); then
+// it waits (bounded) until its own flags[q&1][*] >= q and sums the W slices
+// in rank order — the same order, so the same bits, on every rank.  Two
+// parities suffice: a rank can only reuse a parity after every rank has
+// passed the all-reduce in between.
+static constexpr uint32_t TP_MAX_RANKS = 8;
+inline size_t tp_buffer_bytes(uint32_t world, uint32_t slice) {
+    return (size_t)2 * world * slice * 4 + (size_t)2 * world * 4 + 256;
+}
+
+struct TpPeers {
+    uint8_t* base[TP_MAX_RANKS];  // every rank's buffer, mapped here (own one included)
+};
+
+enum TpOp : int { TP_SUM_F32 = 0, TP_MAX_U64 = 1, TP_GATHER_F32 = 2 };
+
+struct TpArgs {
+    TpPeers peers;
+    void* data;     // in/out: n floats (sum) or one u64 (max); gather: this rank's n floats
+    float* out;     // gather: W * n floats, rank order
+    uint32_t n, rank, world, op, slice;
+};
+
 }  // namespace qb200

@@ -138,6 +138,8 @@ _SIGS = {
     "q_b200_gemv_f32": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_tp_unique_id": (_i, [_vp, _sz]),
     "q_b200_tp_init": (_i, [_vp, _u32, _u32, _vp, _sz]),
+    "q_b200_tp_ipc_handle": (_i, [_vp, _vp, _sz]),
+    "q_b200_tp_ipc_open": (_i, [_vp, _vp, _sz]),
     "q_b200_tp_shape": (_i, [_vp, _u32, _u32, _vp, _u32]),
     "q_b200_kernel_launches": (_u64, []),
     "q_b200_last_error": (C.c_char_p, []),
@@ -221,9 +223,12 @@ def kv_bytes(cfg: q_llama_config) -> int:
 class Model:
     """A model loaded through the upstream API: init -> kv -> arena -> build."""
 
-    def __init__(self, path: str, arena_bytes: int | None = None, tp: tuple | None = None):
+    def __init__(self, path: str, arena_bytes: int | None = None, tp: tuple | None = None,
+                 tp_gather=None):
         """tp = (rank, world, nccl_id bytes) for a tensor-parallel rank (one process per GPU,
-        its device current); the id comes from tp_unique_id() on rank 0."""
+        its device current); the id comes from tp_unique_id() on rank 0.  tp_gather, if given,
+        maps one bytes object per rank to the list of all ranks' (rank order); with it the
+        ranks share CUDA IPC handles and all-reduce over peer memory instead of NCCL."""
         self.ctx = q_context()
         self.model = q_llama_model()
         check(lib.q_init_memory(C.byref(self.ctx), str(path).encode()), "q_init_memory")
@@ -231,6 +236,12 @@ class Model:
             rank, world, uid = tp
             buf = C.create_string_buffer(bytes(uid), len(uid))
             check(lib.q_b200_tp_init(C.byref(self.ctx), rank, world, buf, len(uid)), "q_b200_tp_init")
+            if tp_gather is not None and world > 1:
+                h = C.create_string_buffer(64)
+                check(lib.q_b200_tp_ipc_handle(C.byref(self.ctx), h, 64), "q_b200_tp_ipc_handle")
+                allh = b"".join(tp_gather(h.raw))
+                hb = C.create_string_buffer(allh, len(allh))
+                check(lib.q_b200_tp_ipc_open(C.byref(self.ctx), hb, len(allh)), "q_b200_tp_ipc_open")
         hdr = np.frombuffer((C.c_uint32 * 16).from_address(self.ctx.header), np.uint32)
         cfg = config(int(hdr[2]), int(hdr[3]), int(hdr[4]), int(hdr[5]), int(hdr[6]),
                      int(hdr[7]), int(hdr[8]))

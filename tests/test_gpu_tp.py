@@ -1,6 +1,6 @@
 """Tensor parallelism on 2 GPUs (skipped on single-GPU machines): two ranks,
-one process per GPU, each holding its shard; NCCL all-reduces inside the
-decode graph.  The gathered logits and greedy tokens must match the upstream
+one process per GPU, each holding its shard; the decode graph all-reduces
+either over NVLink peer memory (CUDA IPC) or with NCCL.  The gathered logits and greedy tokens must match the upstream
 kernels' golden outputs for the tiny config (logits max-abs <= 1e-2,
 identical tokens), and each rank's KV cache (its own KV heads) must match
 the CPU oracle's rows for those heads."""
@@ -24,7 +24,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, path, prompt, out):
+def _worker(rank, world, port, path, prompt, ipc, out):
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -33,7 +33,11 @@ def _worker(rank, world, port, path, prompt, out):
     try:
         box = [Q.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
-        m = Q.Model(path, tp=(rank, world, box[0]))
+        def gather(b):
+            allb = [None] * world
+            dist.all_gather_object(allb, b)
+            return allb
+        m = Q.Model(path, tp=(rank, world, box[0]), tp_gather=gather if ipc else None)
         first = m.forward(prompt, 0).copy()
         toks = [int(np.argmax(first))]
         for i in range(31):
@@ -50,7 +54,8 @@ def _worker(rank, world, port, path, prompt, out):
         dist.destroy_process_group()
 
 
-def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden):
+@pytest.mark.parametrize("ipc", [True, False], ids=["peer-memory", "nccl"])
+def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden, ipc):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -59,7 +64,7 @@ def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden):
     q = ctx.Queue()
     port = _free_port()
     prompt = golden["tiny_prompt"]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, tiny_path, prompt, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, tiny_path, prompt, ipc, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
