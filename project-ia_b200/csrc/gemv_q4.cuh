@@ -11,21 +11,23 @@
 // evaluates sum_k q_k x_k EXACTLY on the integer tensor cores: the block's 32
 // inputs are put on a common fixed-point grid (X_k = rint(x_k * 2^(22-e)),
 // e the exponent of the block max, |X_k| < 2^22) and split into three signed
-// int8 limbs (X = a*65536 + b*256 + c); one mma.sync m16n8k32 u8 x s8 -> s32
+// int8 limbs (X = a*65536 + b*256 + c); mma.sync m16n8k32 u8 x s8 -> s32
 // multiplies 16 weight rows (q as u8, no float conversion at all) by the
-// three limb columns with exact int32 sums.  The limbs are recombined and
+// three limb columns with exact int32 sums, two per 32-row slab sharing the
+// limb fragment.  The limbs are recombined and
 // the -8*sum(X) term added in fp32, then scaled by s * 2^-(22-e).  The only
 // approximations are the 2^-23 (relative to the block max) input grid and
 // fp32 accumulation across blocks — the error of an fp32 dot product.
 // Versus dequantising to fp32 this needs ~1.4 instead of ~4 instructions
 // per weight, so the kernel is HBM-bound rather than issue-bound.
 //
-// Device weight layout ("slab tiles"): rows in slabs of 16; for each
-// (slab, block) 320 bytes: 256 bytes of mma A fragments (lane-major, 8 bytes
-// per lane: low nibbles = k 4t..4t+3, high nibbles = k 16+4t..16+4t+3 for
-// rows g and g+8, g = lane/4, t = lane%4) then 16 fp32 scales laid out
-// [g][row g, row g+8].  Blocks of a slab are contiguous, slabs follow each
-// other, so any range of blocks is one 1-D bulk copy.
+// Device weight layout ("slab tiles"): rows in slabs of 32; for each
+// (slab, block) 640 bytes: 512 bytes of mma A fragments (lane-major, 16 bytes
+// per lane: one word per row g, g+8, g+16, g+24 with g = lane/4, t = lane%4,
+// low nibbles = k 4t..4t+3, high nibbles = k 16+4t..16+4t+3) then 32 fp32
+// scales laid out [g][rows g, g+8, g+16, g+24].  Blocks of a slab are
+// contiguous, slabs follow each other, so any range of blocks is one 1-D
+// bulk copy.
 //
 // Work split.  The grid's CTAs take equal contiguous ranges of the block
 // sequence (slab-major), so every CTA streams the same bytes.  A slab cut
@@ -34,7 +36,7 @@
 // Inside a CTA a producer warp streams stages through a shared-memory ring
 // with cp.async.bulk + mbarrier; weight loads start before the programmatic
 // dependent launch wait.  Consumer warp w handles the blocks of a slab with
-// index = w (mod 8), so all sums run in a fixed order (deterministic).
+// index = w (mod warps), so all sums run in a fixed order (deterministic).
 #pragma once
 
 #include "common.cuh"
@@ -61,7 +63,8 @@ struct StepParams {  // device-resident per-step scalars (graph-replay friendly)
 static constexpr int GEMV_CONSUMER_WARPS = QB200_GEMV_CONSUMER_WARPS;
 #define QB200_GEMV_PER_SM_BOUND (QB200_GEMV_CONSUMER_WARPS <= 8 ? 2 : 1)
 static constexpr int GEMV_THREADS = GEMV_CONSUMER_WARPS * 32 + 32;
-static constexpr uint32_t GEMV_BLOCK_BYTES = 320;  // one (slab, block) unit
+static constexpr uint32_t GEMV_SLAB_ROWS = 32;     // rows per slab (two mma row groups)
+static constexpr uint32_t GEMV_BLOCK_BYTES = 640;  // one (slab, block) unit
 static constexpr uint32_t GEMV_BFRAG_BYTES = 128;  // x limb fragments of a block (lanes 0..15; 12..15 zero)
 static constexpr uint32_t GEMV_FSC_BYTES = 32;     // per block: (weight, correction) for t = 0..3
 static constexpr int GEMV_XREGS = 8;               // input float4s per thread per batch
@@ -71,7 +74,7 @@ static constexpr uint32_t GEMV_MAX_NORM_K = GEMV_CONSUMER_WARPS * 32 * GEMV_XREG
 struct GemvArgs {
     const uint8_t* w;          // packed slab tiles
     uint32_t M, K;             // rows, cols
-    uint32_t n_slabs, nb;      // slabs of 16 rows, blocks per row
+    uint32_t n_slabs, nb;      // slabs of 32 rows, blocks per row
     uint32_t max_parts;        // CTAs that can share one slab
     const float* x;            // input vector, or the embedding table if gather
     const StepParams* step;    // per-step scalars (token, pos)
@@ -82,7 +85,7 @@ struct GemvArgs {
     float* y;
     const float* resid;
     int epi;
-    float* part;               // scratch [n_slabs][max_parts][16]
+    float* part;               // scratch [n_slabs][max_parts][32]
     uint32_t* ticket;          // scratch [n_slabs], zero between launches
     // EPI_QKV
     const float* rope_cos;     // [max_seq][hd] duplicated-pair tables
@@ -107,11 +110,11 @@ struct GemvChain {
     unsigned long long* trace;  // step-trace slot (null: off)
 };
 
-// Shared memory: ring | bfrag[max_nb][128] | fsc[max_nb][4] float2 | red[red_slabs][NW][16] | bars | misc
+// Shared memory: ring | bfrag[max_nb][128] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
 __host__ __device__ inline size_t gemv_smem_bytes(uint32_t nb, uint32_t stage_blocks,
                                                   uint32_t n_stage, uint32_t red_slabs) {
     return (size_t)n_stage * stage_blocks * GEMV_BLOCK_BYTES + (size_t)nb * GEMV_BFRAG_BYTES +
-           (size_t)nb * GEMV_FSC_BYTES + (size_t)red_slabs * GEMV_CONSUMER_WARPS * 16 * 4 + 2 * 8 * 8 +
+           (size_t)nb * GEMV_FSC_BYTES + (size_t)red_slabs * GEMV_CONSUMER_WARPS * GEMV_SLAB_ROWS * 4 + 2 * 8 * 8 +
            64 * 4 + 128;
 }
 
@@ -149,8 +152,8 @@ __device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uin
 // Epilogue for lanes 0..15 of one warp holding the 16 finished rows of slab j
 // (lane = row within the slab).  Pairs use the odd lane's value via shuffle.
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uint32_t lane, float v) {
-    const float vn = __shfl_down_sync(0x0000ffffu, v, 1, 16);
-    const uint32_t row = j * 16 + lane;
+    const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+    const uint32_t row = j * GEMV_SLAB_ROWS + lane;
     if (row >= a.M) return;
     if (a.epi == EPI_STORE) {
         a.y[row] = v;
@@ -374,22 +377,24 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     const uint32_t ring_off = 0;
     const uint32_t bfrag_off = (uint32_t)(bfrag - smem) + (lane & 15) * 8;
     const uint32_t fsc_off = (uint32_t)(reinterpret_cast<uint8_t*>(fsc) - smem) + t * 8;
-    // One block: bytes at smem + q (weights, lane part), + sq (scales of
-    // rows g, g+8), + bq (limb fragment), + fq (grid factor, correction).
-    auto block_terms = [&](uint32_t q_off, uint32_t b_off, uint32_t f_off, float2& u, float2& sc) {
-        const uint2 q = *reinterpret_cast<const uint2*>(smem + q_off);
-        sc = *reinterpret_cast<const float2*>(smem + q_off + (256 + g * 8 - lane * 8));
+    // One block of a slab: bytes at smem + q (the lane's 16 weight bytes:
+    // rows g, g+8 for the first mma, g+16, g+24 for the second), + sq (scales
+    // of those four rows), + bq (limb fragment), + fq (grid factor,
+    // correction).  Both mmas share the limb fragment.
+    auto block_terms = [&](uint32_t q_off, uint32_t b_off, uint32_t f_off, float2& u01, float2& u23,
+                           float4& sc) {
+        const uint4 q = *reinterpret_cast<const uint4*>(smem + q_off);
+        sc = *reinterpret_cast<const float4*>(smem + q_off + (512 + g * 16 - lane * 16));
         const uint2 bv = *reinterpret_cast<const uint2*>(smem + b_off);
         const float2 fz = *reinterpret_cast<const float2*>(smem + f_off);
-        int d[4];
-#ifdef QB200_GEMV_NO_MMA  // experiment builds only
-        d[0] = q.x ^ bv.x; d[1] = q.y ^ bv.y; d[2] = (q.x >> 4) ^ bv.y; d[3] = (q.y >> 4) ^ bv.x;
-#else
+        int d[4], e[4];
         mma_u8s8(d, q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, (q.x >> 4) & 0x0F0F0F0Fu,
                  (q.y >> 4) & 0x0F0F0F0Fu, bv.x, bv.y);
-#endif
-        const float2 pv = make_float2((float)(d[0] * m0 + d[1]), (float)(d[2] * m0 + d[3]));
-        u = __ffma2_rn(pv, make_float2(fz.x, fz.x), make_float2(fz.y, fz.y));
+        mma_u8s8(e, q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, (q.z >> 4) & 0x0F0F0F0Fu,
+                 (q.w >> 4) & 0x0F0F0F0Fu, bv.x, bv.y);
+        const float2 fw = make_float2(fz.x, fz.x), fc = make_float2(fz.y, fz.y);
+        u01 = __ffma2_rn(make_float2((float)(d[0] * m0 + d[1]), (float)(d[2] * m0 + d[3])), fw, fc);
+        u23 = __ffma2_rn(make_float2((float)(e[0] * m0 + e[1]), (float)(e[2] * m0 + e[3])), fw, fc);
     };
     // Slab sums wait in red[] (per warp) and are reduced by the whole CTA
     // every red_slabs slabs and at the end: warp w finishes slabs w, w+NW, ...
@@ -401,15 +406,14 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         for (uint32_t r = warp; r < cnt; r += NW) {
             const uint32_t j = j_batch + r;
             float v = 0.0f;
-            if (lane < 16)
 #pragma unroll
-                for (uint32_t w = 0; w < NW; ++w) v += red[(r * NW + w) * 16 + lane];
+            for (uint32_t w = 0; w < NW; ++w) v += red[(r * NW + w) * GEMV_SLAB_ROWS + lane];
             const uint32_t c_first = j == j_first ? own_lo[0] : (j == j_last ? own_lo[1] : cta);
             const uint32_t c_last = j == j_first ? own_hi[0] : (j == j_last ? own_hi[1] : cta);
             bool finish = c_first == c_last;
             if (!finish) {
-                float* pp = a.part + ((size_t)j * a.max_parts) * 16;
-                if (lane < 16) pp[(cta - c_first) * 16 + lane] = v;
+                float* pp = a.part + ((size_t)j * a.max_parts) * GEMV_SLAB_ROWS;
+                pp[(cta - c_first) * GEMV_SLAB_ROWS + lane] = v;
                 __syncwarp();
                 // acq_rel ticket: releases this warp's parts, acquires the others'
                 uint32_t last = 0;
@@ -424,18 +428,17 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     v = 0.0f;
-                    if (lane < 16)
-                        for (uint32_t p = 0; p <= c_last - c_first; ++p) v += __ldcg(&pp[p * 16 + lane]);
+                    for (uint32_t p = 0; p <= c_last - c_first; ++p) v += __ldcg(&pp[p * GEMV_SLAB_ROWS + lane]);
                     if (lane == 0) a.ticket[j] = 0u;
                     finish = true;
                 }
             }
-            if (finish && lane < 16) gemv_epilogue(a, j, lane, v);
+            if (finish) gemv_epilogue(a, j, lane, v);
         }
         j_batch += cnt;
         jl = 0;
     };
-    float2 acc = make_float2(0.0f, 0.0f);  // rows g, g + 8
+    float2 acc = make_float2(0.0f, 0.0f), acc2 = make_float2(0.0f, 0.0f);  // rows g, g+8 | g+16, g+24
     // running ring slot / parity and current slab (no divisions per stage)
     uint32_t j = j_first, jb = j_first * nb;
     for (uint32_t sb0 = x0; sb0 < x1; sb0 += c.stage_blocks) {
@@ -449,35 +452,46 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
 #ifdef QB200_GEMV_NO_COMPUTE  // experiment builds only: stream without arithmetic
             n = 0;
 #endif
-            uint32_t qo = ring_off + s * stage_bytes + (b - sb0) * GEMV_BLOCK_BYTES + lane * 8;
+            uint32_t qo = ring_off + s * stage_bytes + (b - sb0) * GEMV_BLOCK_BYTES + lane * 16;
             uint32_t bo = bfrag_off + (b - jb) * GEMV_BFRAG_BYTES;
             uint32_t fo = fsc_off + (b - jb) * GEMV_FSC_BYTES;
             constexpr uint32_t QS = NW * GEMV_BLOCK_BYTES, BS = NW * GEMV_BFRAG_BYTES, FS = NW * GEMV_FSC_BYTES;
             // four independent blocks per step, accumulated in block order
             for (; n >= 4; n -= 4, qo += 4 * QS, bo += 4 * BS, fo += 4 * FS) {
-                float2 u[4], sc[4];
+                float2 u01[4], u23[4];
+                float4 sc[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) block_terms(qo + i * QS, bo + i * BS, fo + i * FS, u[i], sc[i]);
+                for (int i = 0; i < 4; ++i)
+                    block_terms(qo + i * QS, bo + i * BS, fo + i * FS, u01[i], u23[i], sc[i]);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) acc = __ffma2_rn(sc[i], u[i], acc);
+                for (int i = 0; i < 4; ++i) {
+                    acc = __ffma2_rn(make_float2(sc[i].x, sc[i].y), u01[i], acc);
+                    acc2 = __ffma2_rn(make_float2(sc[i].z, sc[i].w), u23[i], acc2);
+                }
             }
             for (; n > 0; --n, qo += QS, bo += BS, fo += FS) {
-                float2 u, sc;
-                block_terms(qo, bo, fo, u, sc);
-                acc = __ffma2_rn(sc, u, acc);
+                float2 u01, u23;
+                float4 sc;
+                block_terms(qo, bo, fo, u01, u23, sc);
+                acc = __ffma2_rn(make_float2(sc.x, sc.y), u01, acc);
+                acc2 = __ffma2_rn(make_float2(sc.z, sc.w), u23, acc2);
             }
             if (seg_end == jb + nb || seg_end == x1) {
                 // slab j done for this warp: limbs (quad) -> red[jl][warp]
-                float acc0 = acc.x, acc1 = acc.y;
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-                if (t == 0) {
-                    red[(jl * NW + warp) * 16 + g] = acc0;
-                    red[(jl * NW + warp) * 16 + g + 8] = acc1;
+                float r4[4] = {acc.x, acc.y, acc2.x, acc2.y};  // rows g, g+8, g+16, g+24
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    r4[k] += __shfl_xor_sync(0xffffffffu, r4[k], 1);
+                    r4[k] += __shfl_xor_sync(0xffffffffu, r4[k], 2);
                 }
-                acc = make_float2(0.0f, 0.0f);
+                if (t == 0) {
+                    float* rr = red + (jl * NW + warp) * GEMV_SLAB_ROWS;
+                    rr[g] = r4[0];
+                    rr[g + 8] = r4[1];
+                    rr[g + 16] = r4[2];
+                    rr[g + 24] = r4[3];
+                }
+                acc = acc2 = make_float2(0.0f, 0.0f);
                 if (++jl == RS) {
                     reduce_batch(RS);
                     asm volatile("bar.sync 1, %0;" ::"r"(T));  // red[] free again
@@ -510,8 +524,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
     uint8_t* ring = smem;
     uint8_t* bfrag = ring + (size_t)c.n_stage * stage_bytes;
     float2* fsc = reinterpret_cast<float2*>(bfrag + (size_t)c.max_nb * GEMV_BFRAG_BYTES);
-    float* red = reinterpret_cast<float*>(fsc + (size_t)c.max_nb * 4);  // [red_slabs][NW][16]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)c.red_slabs * NW * 16);
+    float* red = reinterpret_cast<float*>(fsc + (size_t)c.max_nb * 4);  // [red_slabs][NW][32]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)c.red_slabs * NW * GEMV_SLAB_ROWS);
     uint64_t* empty = full + 8;
     float* rms_part = reinterpret_cast<float*>(empty + 8);      // [NW]
     const uint32_t tid = threadIdx.x, G = gridDim.x, cta = blockIdx.x, P = c.n_phases;
@@ -616,7 +630,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
 __global__ void q4_pack_kernel(const uint8_t* __restrict__ src, uint32_t M, uint32_t K,
                                uint32_t interleave_half, uint8_t* __restrict__ dst) {
     const uint32_t nb = K / 32;
-    const uint32_t n_slabs = (M + 15) / 16;
+    const uint32_t n_slabs = (M + GEMV_SLAB_ROWS - 1) / GEMV_SLAB_ROWS;
     const uint64_t n = (uint64_t)n_slabs * nb * 32;  // one thread per (slab, block, lane)
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * blockDim.x) {
@@ -625,10 +639,10 @@ __global__ void q4_pack_kernel(const uint8_t* __restrict__ src, uint32_t M, uint
         const uint32_t b = (uint32_t)(sb % nb), j = (uint32_t)(sb / nb);
         const uint32_t g = lane >> 2, t = lane & 3;
         uint8_t* out = dst + sb * GEMV_BLOCK_BYTES;
-        uint32_t words[2];
-        float scales[2];
-        for (int half = 0; half < 2; ++half) {
-            const uint32_t drow = j * 16 + g + 8 * half;
+        uint32_t words[4];
+        float scales[4];
+        for (int quarter = 0; quarter < 4; ++quarter) {  // rows g, g+8, g+16, g+24
+            const uint32_t drow = j * GEMV_SLAB_ROWS + g + 8 * quarter;
             uint32_t wv = 0;
             float sv = 0.0f;
             if (drow < M) {
@@ -643,11 +657,12 @@ __global__ void q4_pack_kernel(const uint8_t* __restrict__ src, uint32_t M, uint
                 }
                 memcpy(&sv, blk + 16, 4);
             }
-            words[half] = wv;
-            scales[half] = sv;
+            words[quarter] = wv;
+            scales[quarter] = sv;
         }
-        *reinterpret_cast<uint2*>(out + lane * 8) = make_uint2(words[0], words[1]);
-        if (t == 0) *reinterpret_cast<float2*>(out + 256 + g * 8) = make_float2(scales[0], scales[1]);
+        *reinterpret_cast<uint4*>(out + lane * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+        if (t == 0)
+            *reinterpret_cast<float4*>(out + 512 + g * 16) = make_float4(scales[0], scales[1], scales[2], scales[3]);
     }
 }
 

@@ -78,7 +78,7 @@ q_error_code check_device_status(const char* where) {
 
 bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
     if (M == 0 || K == 0 || K % 32) return false;
-    const uint32_t nb = K / 32, n_slabs = (M + 15) / 16;
+    const uint32_t nb = K / 32, n_slabs = (M + GEMV_SLAB_ROWS - 1) / GEMV_SLAB_ROWS;
     if (n_slabs > ChainPlan::kTicketWords) return false;
     p.M = M;
     p.K = K;
@@ -119,7 +119,7 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
         if (NB * grid >= (1ull << 32)) return false;  // the kernel's range math is 32-bit
         const uint64_t per_cta = std::max<uint64_t>(1, NB / grid);
         cp.max_parts[i] = (uint32_t)((m.nb + per_cta - 1) / per_cta + 2);
-        cp.part_floats = std::max<size_t>(cp.part_floats, (size_t)m.n_slabs * cp.max_parts[i] * 16);
+        cp.part_floats = std::max<size_t>(cp.part_floats, (size_t)m.n_slabs * cp.max_parts[i] * GEMV_SLAB_ROWS);
         // slabs one CTA's range touches, held in shared memory between
         // CTA-wide reductions (capped: longer ranges reduce in batches)
         const uint64_t range = (NB + grid - 1) / grid;

@@ -48,7 +48,7 @@ struct GemvPlan {
 // A chain of 1..GEMV_MAX_PHASES matrices run by one persistent grid (one
 // CTA per SM).  Scratch layout, shared by every plan: a fixed ticket area of
 // kTicketWords uint32 (zero between launches: each finisher resets its
-// ticket), then the partial sums [n_slabs][max_parts][16] fp32 of the
+// ticket), then the partial sums [n_slabs][max_parts][32] fp32 of the
 // largest phase.
 struct ChainPlan {
     uint32_t n = 0, grid = 0, stage_blocks = 0, n_stage = 0, red_slabs = 0, max_nb = 0;
