@@ -23,15 +23,19 @@
 // through a shared-memory ring — one tiled TMA copy per stage through a
 // tensor map over the whole cache (box = SP rows x hd floats at the cache's
 // row stride; this GPU's own memory, no multicast) — while 8 consumer warps
-//   1. compute scores into shared memory and the chunk max,
-//   | cluster barrier: every CTA reads all chunk maxima over distributed
-//   | shared memory (same order everywhere, so the same global max),
+//   1. compute scores into shared memory and the chunk max, and store that
+//      max into every CTA's shared memory (distributed shared memory),
+//   | cluster barrier: each CTA takes the max of the CS maxima it holds
+//   | (same values, same order everywhere, so the same global max),
 //   2. turn scores into exponentials (upstream's index rule), sum them, and
-//      accumulate partial P.V from the V rows (already streaming in),
+//      accumulate partial P.V from the V rows (already streaming in); store
+//      the sums into every CTA and each 1/CS slice of the partial outputs
+//      into the CTA that finishes that slice,
 //   | cluster barrier,
-//   3. finish a 1/CS slice of the G*hd outputs: sum the CS partials (CTA
+//   3. finish the slice from local shared memory: sum the CS partials (CTA
 //      order) and multiply by 1/L.
-//   | cluster barrier (no CTA leaves while others read its shared memory).
+// No CTA touches another's shared memory after the second barrier, so CTAs
+// may leave as soon as they are done.
 // Rows older than the current position do not depend on the previous kernel
 // and are copied before the programmatic-dependency wait; the current row
 // (written by the QKV epilogue just before) is copied after it.
@@ -62,12 +66,11 @@ struct AttnArgs {
     unsigned long long* trace;  // step-trace slot (null: off)
 };
 
-// ring[slots][16 KB] | sc[G][chunk_alloc] | ored[PG][G][hd] | opart[G][hd]
+// ring[slots][16 KB] | sc[G][chunk_alloc] | ored[PG][G][hd]
 __host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t hd, uint32_t chunk_alloc,
                                                   uint32_t slots) {
     const uint32_t PG = (ATT_CWARPS * 32) / (hd / 4);
-    return (size_t)slots * ATT_STAGE_BYTES + (size_t)G * chunk_alloc * 4 + (size_t)PG * G * hd * 4 +
-           (size_t)G * hd * 4;
+    return (size_t)slots * ATT_STAGE_BYTES + (size_t)G * chunk_alloc * 4 + (size_t)PG * G * hd * 4;
 }
 
 // Whole-warp calls only (.aligned): each reconverges its warp first.
@@ -91,13 +94,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* m
         : "memory");
 }
 
-// A float in CTA `rank`'s shared memory, at the address `p` has in ours.
-__device__ __forceinline__ float ld_dsmem(const float* p, uint32_t rank) {
+// Store into CTA `rank`'s shared memory, at the address `p` has in ours.
+__device__ __forceinline__ void st_dsmem(float* p, uint32_t rank, float v) {
     uint32_t ra;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem4(float* p, uint32_t rank, float4 v) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 
 #ifdef QB200_ATTN_PHASES  // experiment builds only: per-CTA phase timestamps
@@ -127,7 +135,11 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[ATT_MAX_SLOTS], empty[ATT_MAX_SLOTS];
     __shared__ float wred[NW][ATT_MAXG];
-    __shared__ float cm[ATT_MAXG], gmx[ATT_MAXG], lsum[ATT_MAXG], linv[ATT_MAXG];
+    __shared__ float gmx[ATT_MAXG], linv[ATT_MAXG];
+    // filled by the other CTAs of the cluster (pushed before each cluster barrier)
+    __shared__ float cmx[16][ATT_MAXG];                    // chunk maxima, by source CTA
+    __shared__ float lgath[16][ATT_MAXG];                  // exponential sums, by source CTA
+    __shared__ __align__(16) float pgath[ATT_MAXG * 128 + 16];  // [CS][per] partial outputs of my slice
 
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t CS = gridDim.x, r = blockIdx.x, h = blockIdx.y;  // cluster = one grid row
@@ -135,7 +147,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     uint8_t* ring = smem;
     float* sc = reinterpret_cast<float*>(smem + (size_t)SL * ATT_STAGE_BYTES);  // [G][CA]
     float4* ored = reinterpret_cast<float4*>(sc + (size_t)G * CA);              // [PG][G][VQ]
-    float* opart = reinterpret_cast<float*>(ored + (size_t)PG * G * VQ);        // [G][HD]
 
     if (tid == 0) {
         trace_mark(a.trace, 0);
@@ -195,8 +206,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
             g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + 7] = smid;
         }
 #endif
-        cluster_wait();
-        cluster_arrive();
         cluster_wait();
         cluster_arrive();
         cluster_wait();
@@ -276,10 +285,12 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
             if (lane == 0) wred[warp][g] = m;
         }
         asm volatile("bar.sync 1, %0;" ::"r"(T));
-        if (tid < G) {
+        // push this chunk's max of each query head to every CTA of the cluster
+        for (uint32_t i = tid; i < CS * G; i += T) {
+            const uint32_t g = i % G;
             float m = -INFINITY;
-            for (int w = 0; w < NW; ++w) m = fmaxf(m, wred[w][tid]);
-            cm[tid] = m;
+            for (int w = 0; w < NW; ++w) m = fmaxf(m, wred[w][g]);
+            st_dsmem(&cmx[r][g], i / G, m);
         }
     }
     if (tid == 0) ATTN_PHASE(2);
@@ -290,7 +301,7 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     // phase 2: global max, exponentials (upstream index rule), sums, partial P.V
     if (tid < G) {
         float m = -INFINITY;
-        for (uint32_t rr = 0; rr < CS; ++rr) m = fmaxf(m, ld_dsmem(&cm[tid], rr));
+        for (uint32_t rr = 0; rr < CS; ++rr) m = fmaxf(m, cmx[rr][tid]);
         gmx[tid] = m;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
@@ -306,7 +317,8 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
         float l = 0.0f;
         for (uint32_t pp = lane; pp < len; pp += 32) l += sc[warp * CA + pp];
         l = warp_sum(l);
-        if (lane == 0) lsum[warp] = l;
+        // push this chunk's sum to every CTA
+        for (uint32_t rr = lane; rr < CS; rr += 32) st_dsmem(&lgath[r][warp], rr, l);
     }
     {
         const uint32_t dq = tid % VQ, pg = tid / VQ;
@@ -352,7 +364,9 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
                 acc.z += t.z;
                 acc.w += t.w;
             }
-            reinterpret_cast<float4*>(opart)[i] = acc;  // i = g * VQ + column
+            // outputs 4i..4i+3 belong to CTA 4i / per (per is a multiple of 8)
+            const uint32_t per = G * HD / CS, o = 4 * i;
+            st_dsmem4(&pgath[r * per + o % per], o / per, acc);
         }
     }
     if (tid == 0) ATTN_PHASE(4);
@@ -360,33 +374,23 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     cluster_wait();
     if (tid == 0) ATTN_PHASE(5);
 
-    // phase 3: this CTA's slice of the outputs.  Every partial of the slice
-    // is fetched at once (one DSMEM load per thread and source CTA), then
-    // summed in CTA order.
+    // phase 3: this CTA's slice of the outputs, from the partials and sums
+    // every CTA pushed here (summed in CTA order)
     {
-        const uint32_t total = G * HD, per = (total + CS - 1) / CS;
-        const uint32_t o0 = min(r * per, total), o1 = min(o0 + per, total), n = o1 - o0;
-        float* gath = reinterpret_cast<float*>(ored);  // [CS][per] + [CS][G]; phase 2 is done with ored
-        for (uint32_t i = tid; i < CS * n; i += T) {
-            const uint32_t rr = i / n, k = i % n;
-            gath[rr * per + k] = ld_dsmem(&opart[o0 + k], rr);
-        }
-        for (uint32_t i = tid; i < CS * G; i += T) gath[CS * per + i] = ld_dsmem(&lsum[i % G], i / G);
-        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        const uint32_t per = G * HD / CS, o0 = r * per;
         if (tid < G) {
             float l = 0.0f;
-            for (uint32_t rr = 0; rr < CS; ++rr) l += gath[CS * per + rr * G + tid];
+            for (uint32_t rr = 0; rr < CS; ++rr) l += lgath[rr][tid];
             linv[tid] = __fdiv_rn(1.0f, l);
         }
         asm volatile("bar.sync 1, %0;" ::"r"(T));
-        for (uint32_t k = tid; k < n; k += T) {
+        for (uint32_t k = tid; k < per; k += T) {
             float acc = 0.0f;
-            for (uint32_t rr = 0; rr < CS; ++rr) acc += gath[rr * per + k];
+            for (uint32_t rr = 0; rr < CS; ++rr) acc += pgath[rr * per + k];
             a.out[(size_t)h * G * HD + o0 + k] = __fmul_rn(acc, linv[(o0 + k) / HD]);
         }
     }
-    cluster_arrive();  // nobody leaves while its shared memory may still be read
-    cluster_wait();
+    // (no shared memory of another CTA is touched after the second barrier)
     if (tid == 0) trace_mark(a.trace, 2);
     if (tid == 0) ATTN_PHASE(6);
 }
