@@ -205,7 +205,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["gemv"], help="time one kernel alone (profiling runs)")
+    ap.add_argument("--only", choices=["gemv", "attention"],
+                    help="profiling runs: the gate/up GEMV alone, or a few decode steps of a "
+                         "2-layer 8B-shaped model (small vocab) over a 2048-position cache")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -243,6 +245,16 @@ def main():
     if args.only == "gemv":
         import qorus_b200 as Q
         print(json.dumps(gemv_roofline(Q, torch, 6450.9)), flush=True)
+        return
+    if args.only == "attention":
+        import qorus_b200 as Q
+        small = Q.config(4096, CFG8B["dim"], CFG8B["hidden"], 2, CFG8B["heads"], CFG8B["kv_heads"], 4096)
+        spath = str(Path(model_path(4096)).with_name("qorus_llama3_8b_2layer_small.qorus"))
+        Q.write_model(spath, small, seed=SEED, threads=0)
+        ms = Q.Model(spath)
+        ms.kv_write(kv_image(Q, small))
+        toks = ms.decode_loop(1, PREFILL, max(4, args.steps), sync=True)
+        print(json.dumps({"only": "attention", "steps": int(len(toks))}), flush=True)
         return
     dist = None
     if world > 1:
