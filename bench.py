@@ -134,7 +134,7 @@ class Clocks:
 
 # DRAM bytes (read + write) of one gate/up launch, from an ncu capture of
 # `bench.py --only gemv` (profiles/gemv_q4_gate_up_28672x4096.txt).
-GEMV_GU_TRAFFIC = 74_420_992
+GEMV_GU_TRAFFIC = 73_896_192
 
 
 def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
