@@ -189,9 +189,25 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uin
 }
 
 #ifdef QB200_CHAIN_TS  // experiment builds only: per-CTA phase timestamps
-__device__ unsigned long long g_chain_ts[256 * 20];
+__device__ unsigned long long g_chain_ts[4 * 256 * 20];
+// one record per matrix shape class (QKV, wo, gate/up, other), so the last
+// launch of each class in a decode step stays readable
+__device__ __forceinline__ uint32_t chain_ts_kind(const GemvChain& c) {
+    const uint32_t M = c.ph[0].M, K = c.ph[0].K;
+    return M == 28672 ? 2u : (K == 4096 && M == 4096) ? 1u : (K == 4096 ? 0u : 3u);
+}
+__device__ __forceinline__ unsigned long long gtimer_fenced() {
+    unsigned long long t;
+#ifdef QB200_CHAIN_TS_CLOCK  // SM cycle counter: exact within a CTA, not comparable across CTAs
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t)::"memory");
+#else
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
+#endif
+    return t;
+}
+__shared__ uint32_t s_ts_base;  // record offset of this CTA, set at kernel entry
 #define CHAIN_TS(i) \
-    if (threadIdx.x == 0) g_chain_ts[blockIdx.x * 20 + (i)] = gtimer()
+    if (threadIdx.x == 0) g_chain_ts[s_ts_base + (i)] = gtimer_fenced()
 #else
 #define CHAIN_TS(i) ((void)0)
 #endif
@@ -202,6 +218,34 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
     return v;
 }
 
+// This CTA's share of one phase: blocks [x0, x1) of the slab-major
+// sequence, its first and last slab, and for those two slabs the lowest and
+// highest CTA that holds part of them (equal to this CTA when unshared).
+// Computed before the dependency wait: the divisions by the grid size form
+// a dependent chain of a few thousand cycles.
+struct PhaseRange {
+    uint32_t x0, x1, j_first, j_last;
+    uint32_t own_lo[2], own_hi[2];  // [first slab, last slab]
+};
+
+__device__ inline PhaseRange phase_range(uint32_t n_slabs, uint32_t nb, uint32_t cta, uint32_t G) {
+    PhaseRange r;
+    const uint32_t NB = n_slabs * nb;
+    r.x0 = range_begin(NB, cta, G);
+    r.x1 = range_begin(NB, cta + 1, G);
+    r.j_first = r.x0 / nb;
+    r.j_last = r.x1 > r.x0 ? (r.x1 - 1) / nb : r.j_first;
+    r.own_lo[0] = r.own_lo[1] = r.own_hi[0] = r.own_hi[1] = cta;
+    if (r.x1 > r.x0) {
+        if (r.j_first * nb < r.x0 || (r.j_first + 1) * nb > r.x1) {
+            r.own_lo[0] = cta_of(NB, G, r.j_first * nb);
+            r.own_hi[0] = cta_of(NB, G, r.j_first * nb + nb - 1);
+        }
+        if (r.j_last != r.j_first && (r.j_last + 1) * nb > r.x1) r.own_hi[1] = cta_of(NB, G, r.j_last * nb + nb - 1);
+    }
+    return r;
+}
+
 // One GEMV (chain phase) for this CTA's range: input prologue, main loop over
 // the ring (slot s / parity ph carried across phases), slab reductions,
 // split-slab finish and epilogue.  Consumer threads only (T of them).
@@ -209,34 +253,25 @@ template <uint32_t NW>
 __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c, uint8_t* smem,
                                            uint8_t* bfrag, float2* fsc, float* red, uint64_t* full,
                                            uint64_t* empty, float* rms_part, uint32_t& s,
-                                           uint32_t& ph, uint32_t pidx) {
+                                           uint32_t& ph, uint32_t pidx, bool dry,
+                                           const PhaseRange& r) {
     constexpr uint32_t T = NW * 32;
+    if (!dry && pidx == 0) CHAIN_TS(6);
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t G = gridDim.x, cta = blockIdx.x;
+    const uint32_t cta = blockIdx.x;
     const uint32_t nb = a.nb;
     const uint32_t stage_bytes = c.stage_blocks * GEMV_BLOCK_BYTES;
-    const uint32_t NB = a.n_slabs * nb;
-    const uint32_t x0 = range_begin(NB, cta, G), x1 = range_begin(NB, cta + 1, G);
+    const uint32_t x0 = r.x0, x1 = r.x1;
     if (x0 >= x1) return;  // (host keeps G <= NB, so never taken)
-    // Only the first and last slab of the range can be shared with other
-    // CTAs; resolve their owners once, here.
-    const uint32_t j_first = x0 / nb, j_last = (x1 - 1) / nb;
-    uint32_t own_lo[2] = {cta, cta}, own_hi[2] = {cta, cta};  // [first slab, last slab]
-    if (j_first * nb < x0 || (j_first + 1) * nb > x1) {
-        own_lo[0] = cta_of(NB, G, j_first * nb);
-        own_hi[0] = cta_of(NB, G, j_first * nb + nb - 1);
-    }
-    if (j_last != j_first && (j_last + 1) * nb > x1) {
-        own_lo[1] = cta;
-        own_hi[1] = cta_of(NB, G, j_last * nb + nb - 1);
-    }
+    const uint32_t j_first = r.j_first, j_last = r.j_last;
+    const uint32_t own_lo[2] = {r.own_lo[0], r.own_lo[1]}, own_hi[2] = {r.own_hi[0], r.own_hi[1]};
 
     // ---- input prologue ------------------------------------------------------------
     const uint32_t tsb = 4 * pidx;
     (void)tsb;
-    CHAIN_TS(tsb + 0);
+    if (!dry) CHAIN_TS(tsb + 0);
     const float* xs = a.x;
-    if (a.gather) xs = a.x + (size_t)a.step->token * a.K;
+    if (a.gather) xs = a.x + (size_t)(dry ? 0u : a.step->token) * a.K;
     // All input loads are issued at once (float4, registers); a serial loop
     // of dependent L2 loads here would delay the whole stream by microseconds.
     // Thread tid holds float4 number tid + T*r; 8 consecutive threads hold
@@ -254,7 +289,18 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
             xv[r] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             gv[r] = (g4 && i < n4) ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (a.x_copy && cta == 0) {
+#ifdef QB200_CHAIN_TS
+        if (tid == 0 && base == 0 && pidx == 0 && !dry) {
+            unsigned long long t;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.eq.f32 p, %1, 0f7F7FFFFF;\n\t"
+                "@p st.volatile.global.u32 [%2], 0;\n\t}"
+                ::"l"(0ull), "f"(xv[0].x), "l"(g_chain_ts + 5119) : "memory");
+            t = gtimer_fenced();
+            g_chain_ts[s_ts_base + 8] = t;
+        }
+#endif
+        if (a.x_copy && cta == 0 && !dry) {
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
                 const uint32_t i = base + tid + T * r;
@@ -364,6 +410,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
+    if (dry) return;
     CHAIN_TS(tsb + 1);
 
     // ---- main loop ---------------------------------------------------------------
@@ -441,8 +488,11 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     float2 acc = make_float2(0.0f, 0.0f), acc2 = make_float2(0.0f, 0.0f);  // rows g, g+8 | g+16, g+24
     // running ring slot / parity and current slab (no divisions per stage)
     uint32_t j = j_first, jb = j_first * nb;
+    if (pidx == 0) CHAIN_TS(10);
     for (uint32_t sb0 = x0; sb0 < x1; sb0 += c.stage_blocks) {
+        if (sb0 == x0 && pidx == 0) CHAIN_TS(11);
         mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
+        if (sb0 == x0 && pidx == 0) CHAIN_TS(15);
         const uint32_t sb1 = min(sb0 + c.stage_blocks, x1);
         for (uint32_t seg = sb0; seg < sb1;) {
             const uint32_t seg_end = min(sb1, jb + nb);
@@ -537,8 +587,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
         }
         fence_mbar_init();
     }
+    // The phases' arguments, copied to shared memory before the dependency
+    // wait: c.ph[p] with a run-time p is a generic load from the parameter
+    // window, slow enough (about a microsecond per dependent chain) to show
+    // on the critical path after the wait; shared-memory reads are not.
+    __shared__ GemvArgs s_args[GEMV_MAX_PHASES];
+    {
+        static_assert(sizeof(GemvArgs) % 8 == 0, "GemvArgs copied as 64-bit words");
+        constexpr uint32_t WORDS = sizeof(GemvArgs) / 8;
+        const uint64_t* src = reinterpret_cast<const uint64_t*>(c.ph);
+        uint64_t* dst = reinterpret_cast<uint64_t*>(s_args);
+        for (uint32_t i = tid; i < P * WORDS; i += blockDim.x) dst[i] = src[i];
+    }
+    __shared__ PhaseRange s_rng[GEMV_MAX_PHASES];
+    if (tid < P) s_rng[tid] = phase_range(c.ph[tid].n_slabs, c.ph[tid].nb, cta, G);
+#ifdef QB200_CHAIN_TS
+    if (tid == 0) s_ts_base = chain_ts_kind(c) * 5120 + blockIdx.x * 20;
+#endif
     __syncthreads();
     if (tid == 0) trace_mark(c.trace, 0);
+    CHAIN_TS(12);
     pdl_trigger();
 
     if (tid >= T) {
@@ -552,10 +620,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
                 if (p > 0)
                     while (ld_acquire_u32(c.bar + p - 1) < G) __nanosleep(32);
 #endif
-                const GemvArgs& a = c.ph[p];
-                const uint32_t NB = a.n_slabs * a.nb;
-                const uint32_t x0 = range_begin(NB, cta, G), x1 = range_begin(NB, cta + 1, G);
+                const GemvArgs& a = s_args[p];
+                const uint32_t x0 = s_rng[p].x0, x1 = s_rng[p].x1;
                 for (uint32_t b0 = x0; b0 < x1; b0 += c.stage_blocks, ++k) {
+#ifdef QB200_PREWAIT_STAGES  // experiment builds only: fewer weight stages before the dependency wait
+                    if (k == QB200_PREWAIT_STAGES) pdl_wait();
+#endif
                     if (k >= c.n_stage && !mbar_wait(&empty[s], ph ^ 1, QDEV_WAIT_EMPTY_TIMEOUT)) {
                         ok = false;
                         break;
@@ -575,17 +645,43 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
                     }
                 }
             }
+#ifdef QB200_CHAIN_TS
+            g_chain_ts[s_ts_base + 14] = gtimer_fenced();
+#endif
         }
+#ifdef QB200_CHAIN_TS
+        if (tid == T + 1 && mbar_wait(&full[0], 0, QDEV_WAIT_FULL_TIMEOUT))
+            g_chain_ts[s_ts_base + 13] = gtimer_fenced();
+#endif
         pdl_wait();  // every thread waits: the grid ends after its predecessor
         return;
     }
 
     // ---- consumers -----------------------------------------------------------------
-    pdl_wait();
-    if (tid == 0) trace_mark(c.trace, 1);
-    CHAIN_TS(16);
+#ifdef QB200_WARM_PARAMS  // experiment builds only: touch every parameter line before the wait
+    {
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&c);
+        uint32_t v = 0;
+        for (uint32_t i = tid; i < sizeof(GemvChain) / 4; i += T) v ^= pw[i];
+        if (v == 0x9e3779b9u && c.trace == nullptr && c.n_phases == 77) qdev_fail(99);
+    }
+#endif
     uint32_t s = 0, ph = 0;
-    for (uint32_t p = 0; p < P; ++p) {
+#ifdef QB200_GEMV_DRY_PROLOGUE  // experiment builds only: a discarded prologue pass before the wait
+    constexpr uint32_t it0 = 0;
+#else
+    constexpr uint32_t it0 = 1;
+#endif
+#pragma unroll 1
+    for (uint32_t it = it0; it <= P; ++it) {
+        const bool dry = it == 0;
+        const uint32_t p = dry ? 0u : it - 1;
+        if (it == 1) {
+            pdl_wait();
+            if (tid == 0) trace_mark(c.trace, 1);
+            CHAIN_TS(16);
+            CHAIN_TS(7);
+        }
         if (p > 0) {
             // grid barrier: every CTA has finished phase p - 1 (outputs written)
             if (tid == 0) {
@@ -603,7 +699,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
             if (p == 2) CHAIN_TS(19);
             asm volatile("bar.sync 1, %0;" ::"r"(T));
         }
-        gemv_phase<NW>(c.ph[p], c, smem, bfrag, fsc, red, full, empty, rms_part, s, ph, p);
+        gemv_phase<NW>(s_args[p], c, smem, bfrag, fsc, red, full, empty, rms_part, s, ph, p, dry, s_rng[p]);
+        if (dry) continue;
         if (p == 1) CHAIN_TS(18);
         if (p + 1 < P && tid == 0) {
             // consumers passed bar.sync at the end of the phase, so this

@@ -54,6 +54,13 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lk(mu);
     if (done.count({kernel, dev})) return cudaSuccess;
+    // the opt-in limit covers static + dynamic shared memory
+    cudaFuncAttributes fa{};
+    int optin = 0;
+    if ((e = cudaFuncGetAttributes(&fa, kernel)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+        return e;
+    bytes = std::min(bytes, optin - (int)fa.sharedSizeBytes);
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e == cudaSuccess) done.insert({kernel, dev});
     return e;
