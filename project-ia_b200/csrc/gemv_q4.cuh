@@ -65,11 +65,15 @@ static constexpr int GEMV_CONSUMER_WARPS = QB200_GEMV_CONSUMER_WARPS;
 static constexpr int GEMV_THREADS = GEMV_CONSUMER_WARPS * 32 + 32;
 static constexpr uint32_t GEMV_SLAB_ROWS = 32;     // rows per slab (two mma row groups)
 static constexpr uint32_t GEMV_BLOCK_BYTES = 640;  // one (slab, block) unit
-static constexpr uint32_t GEMV_BFRAG_BYTES = 128;  // x limb fragments of a block (lanes 0..15; 12..15 zero)
+// x limb fragments of a block: 128 bytes (lanes 0..15; 12..15 zero) in a
+// 144-byte row, so that 32 threads writing or reading the same 16-byte
+// column of 32 consecutive rows touch every bank (a 128-byte stride would
+// put them all on the same four banks).
+static constexpr uint32_t GEMV_BFRAG_BYTES = 144;
 static constexpr uint32_t GEMV_FSC_BYTES = 32;     // per block: (weight, correction) for t = 0..3
-static constexpr int GEMV_XREGS = 8;               // input float4s per thread per batch
-// An RMSNorm prologue needs the whole input in one register batch.
-static constexpr uint32_t GEMV_MAX_NORM_K = GEMV_CONSUMER_WARPS * 32 * GEMV_XREGS * 4;
+// An RMSNorm prologue needs the whole input in one pass: one 32-value block
+// per consumer thread.
+static constexpr uint32_t GEMV_MAX_NORM_K = GEMV_CONSUMER_WARPS * 32 * 32;
 
 struct GemvArgs {
     const uint8_t* w;          // packed slab tiles
@@ -110,7 +114,7 @@ struct GemvChain {
     unsigned long long* trace;  // step-trace slot (null: off)
 };
 
-// Shared memory: ring | bfrag[max_nb][128] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
+// Shared memory: ring | bfrag[max_nb][144] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
 __host__ __device__ inline size_t gemv_smem_bytes(uint32_t nb, uint32_t stage_blocks,
                                                   uint32_t n_stage, uint32_t red_slabs) {
     return (size_t)n_stage * stage_blocks * GEMV_BLOCK_BYTES + (size_t)nb * GEMV_BFRAG_BYTES +
@@ -272,22 +276,24 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     if (!dry) CHAIN_TS(tsb + 0);
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)(dry ? 0u : a.step->token) * a.K;
-    // All input loads are issued at once (float4, registers); a serial loop
-    // of dependent L2 loads here would delay the whole stream by microseconds.
-    // Thread tid holds float4 number tid + T*r; 8 consecutive threads hold
-    // one 32-element Q4 block.
-    constexpr int NR = GEMV_XREGS;
-    const uint32_t n4 = a.K / 4;
+    // Two steps.  (1) Coalesced: thread tid loads float4 number tid + T*r
+    // (all loads issued together), applies the RMSNorm, and parks the
+    // values in the limb-table area, block b's 128 bytes at the start of
+    // its row.  (2) Thread tid converts blocks tid, tid + T, ...: the
+    // 32 values of a block in its registers, so the block maximum, the limb
+    // bytes and the integer sum need no cross-lane steps; it overwrites the
+    // block's own row with the limb fragment.
+    const uint32_t nbk = a.K / 32, n4 = a.K / 4;
     const float4* x4 = reinterpret_cast<const float4*>(xs);
     const float4* g4 = reinterpret_cast<const float4*>(a.norm_w);
+    constexpr int NR = 8;
     float r_norm = 1.0f;
     for (uint32_t base = 0; base < n4; base += T * NR) {
-        float4 xv[NR], gv[NR];
+        float4 xv[NR];
 #pragma unroll
         for (int r = 0; r < NR; ++r) {
             const uint32_t i = base + tid + T * r;
             xv[r] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            gv[r] = (g4 && i < n4) ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #ifdef QB200_CHAIN_TS
         if (tid == 0 && base == 0 && pidx == 0 && !dry) {
@@ -307,107 +313,125 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
                 if (i < n4) reinterpret_cast<float4*>(a.x_copy)[i] = xv[r];
             }
         }
-        if (a.norm_w && base == 0) {
-            // upstream rmsnorm.c: mean of squares, rsqrt + one Newton step
-            // (the host only pairs a norm with K <= T*NR*4, one batch)
-            float ss = 0.0f;
+        if (a.norm_w) {
+            float4 gv[NR];
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
-                ss = __fmaf_rn(xv[r].x, xv[r].x, ss);
-                ss = __fmaf_rn(xv[r].y, xv[r].y, ss);
-                ss = __fmaf_rn(xv[r].z, xv[r].z, ss);
-                ss = __fmaf_rn(xv[r].w, xv[r].w, ss);
+                const uint32_t i = base + tid + T * r;
+                gv[r] = i < n4 ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            ss = warp_sum(ss);
-            if (lane == 0) rms_part[warp] = ss;
-            asm volatile("bar.sync 1, %0;" ::"r"(T));
-            float tot = 0.0f;
-            for (uint32_t i = 0; i < NW; ++i) tot += rms_part[i];
-            float me = __fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps);
-            float r0 = __fdiv_rn(1.0f, __fsqrt_rn(me));
-            float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0, r0)));
-            r_norm = __fmul_rn(__fmul_rn(r0, tm), 0.5f);
+            if (base == 0) {
+                // upstream rmsnorm.c: mean of squares, rsqrt + one Newton step
+                // (the host only pairs a norm with K <= T*NR*4, one pass)
+                float ss = 0.0f;
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    ss = __fmaf_rn(xv[r].x, xv[r].x, ss);
+                    ss = __fmaf_rn(xv[r].y, xv[r].y, ss);
+                    ss = __fmaf_rn(xv[r].z, xv[r].z, ss);
+                    ss = __fmaf_rn(xv[r].w, xv[r].w, ss);
+                }
+                ss = warp_sum(ss);
+                if (lane == 0) rms_part[warp] = ss;
+                asm volatile("bar.sync 1, %0;" ::"r"(T));
+                float tot = 0.0f;
+                for (uint32_t w = 0; w < NW; ++w) tot += rms_part[w];
+                const float me = __fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps);
+                const float r0 = __fdiv_rn(1.0f, __fsqrt_rn(me));
+                const float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0, r0)));
+                r_norm = __fmul_rn(__fmul_rn(r0, tm), 0.5f);
+            }
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                xv[r].x = __fmul_rn(__fmul_rn(xv[r].x, r_norm), gv[r].x);
+                xv[r].y = __fmul_rn(__fmul_rn(xv[r].y, r_norm), gv[r].y);
+                xv[r].z = __fmul_rn(__fmul_rn(xv[r].z, r_norm), gv[r].z);
+                xv[r].w = __fmul_rn(__fmul_rn(xv[r].w, r_norm), gv[r].w);
+            }
         }
-        // Fixed-point limbs: B fragment of lane L = g*4 + t (g < 3 = limb):
-        // word 0 = limb g of k 4t..4t+3, word 1 = limb g of k 16+4t..16+4t+3.
-        // This thread's float4 is k = 4*sub..4*sub+3 of its block, i.e.
-        // t = sub % 4, word = sub / 4: one 32-bit store per limb.
 #pragma unroll
         for (int r = 0; r < NR; ++r) {
             const uint32_t i = base + tid + T * r;
-            if (base + T * r >= n4) break;  // uniform: whole warp past the end
-            float4 v = xv[r];
-            if (a.norm_w) {
-                v.x = __fmul_rn(__fmul_rn(v.x, r_norm), gv[r].x);
-                v.y = __fmul_rn(__fmul_rn(v.y, r_norm), gv[r].y);
-                v.z = __fmul_rn(__fmul_rn(v.z, r_norm), gv[r].z);
-                v.w = __fmul_rn(__fmul_rn(v.w, r_norm), gv[r].w);
-            }
-            float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            // Grid 2^-sh with sh = 22 - e, m = f 2^e (f in [0.5, 1)): for a
-            // normal m, e = E - 126 with E its biased exponent field.  A
-            // subnormal m uses E = 1 (a coarser grid, still |X| <= 2^22), an
-            // all-zero block any E.  v 2^sh is formed as two exact
-            // power-of-two products (sh spans -106..147); an intermediate
-            // can only lose bits when the final value rounds to 0 anyway.
-            const int E = m > 0.0f ? max((int)(__float_as_uint(m) >> 23), 1) : 126;
-            const int sh = 148 - E;
-            int X[4];
-            if (sh <= 127) {  // one exact product (every block but the tiniest)
-                const float p = __int_as_float((sh + 127) << 23);
-                X[0] = __float2int_rn(__fmul_rn(v.x, p));
-                X[1] = __float2int_rn(__fmul_rn(v.y, p));
-                X[2] = __float2int_rn(__fmul_rn(v.z, p));
-                X[3] = __float2int_rn(__fmul_rn(v.w, p));
-            } else {
-                const int s1 = sh >> 1, s2 = sh - s1;
-                const float p1 = __int_as_float((s1 + 127) << 23), p2 = __int_as_float((s2 + 127) << 23);
-                X[0] = __float2int_rn(__fmul_rn(__fmul_rn(v.x, p1), p2));
-                X[1] = __float2int_rn(__fmul_rn(__fmul_rn(v.y, p1), p2));
-                X[2] = __float2int_rn(__fmul_rn(__fmul_rn(v.z, p1), p2));
-                X[3] = __float2int_rn(__fmul_rn(__fmul_rn(v.w, p1), p2));
-            }
-            // Balanced limbs X = 65536 a + 256 b + c, b and c in [-128, 128):
-            // c = X mod 256 (as a signed byte), b = floor((X + 128) / 256)
-            // mod 256, a = floor((X + 32896) / 65536), i.e. byte 0 of X,
-            // byte 1 of X + 0x80 and byte 2 of X + 0x8080; gathered four
-            // elements at a time with byte permutes.
-            const uint32_t Y[4] = {(uint32_t)X[0] + 0x80u, (uint32_t)X[1] + 0x80u, (uint32_t)X[2] + 0x80u,
-                                   (uint32_t)X[3] + 0x80u};
-            const uint32_t Z[4] = {Y[0] + 0x8000u, Y[1] + 0x8000u, Y[2] + 0x8000u, Y[3] + 0x8000u};
-            const uint32_t lc = __byte_perm(__byte_perm((uint32_t)X[0], (uint32_t)X[1], 0x0040),
-                                            __byte_perm((uint32_t)X[2], (uint32_t)X[3], 0x0040), 0x5410);
-            const uint32_t lb = __byte_perm(__byte_perm(Y[0], Y[1], 0x0051), __byte_perm(Y[2], Y[3], 0x0051),
-                                            0x5410);
-            const uint32_t la = __byte_perm(__byte_perm(Z[0], Z[1], 0x0062), __byte_perm(Z[2], Z[3], 0x0062),
-                                            0x5410);
-            int sx = (X[0] + X[1]) + (X[2] + X[3]);
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
             if (i < n4) {
-                const uint32_t b = i / 8, sub = i % 8;
-                uint32_t* bf = reinterpret_cast<uint32_t*>(bfrag + (size_t)b * GEMV_BFRAG_BYTES);
-                const uint32_t w = (sub % 4) * 2 + sub / 4;  // 32-bit word within a limb's 32 B
-                bf[0 * 8 + w] = la;
-                bf[1 * 8 + w] = lb;
-                bf[2 * 8 + w] = lc;
-                bf[3 * 8 + w] = 0u;  // column 3 (B lanes 12..15) is zero
-                if (sub == 0) {
-                    // 2^-sh = 2^(E-148): normal for E >= 22, else the
-                    // subnormal 2^(E+1) * 2^-149
-                    const float f = __uint_as_float(E >= 22 ? (uint32_t)(E - 21) << 23
-                                                            : 1u << (E + 1));
-                    // lane t of the D fragment: t = 0 weighs 256*D_a + D_b by
-                    // 256 f; t = 1 weighs D_c by f and adds the -8*sum(X)
-                    // correction; t = 2, 3 carry no limb and weigh 0
-                    float4* fs = reinterpret_cast<float4*>(fsc + (size_t)b * 4);
-                    fs[0] = make_float4(f * 256.0f, 0.0f, f, f * (-8.0f * (float)sx));
-                    fs[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                }
+                const uint32_t b = i / 8, q = i % 8;
+                *reinterpret_cast<float4*>(bfrag + (size_t)b * GEMV_BFRAG_BYTES + q * 16) = xv[r];
             }
         }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
+    if (!dry && pidx == 0) CHAIN_TS(9);
+    for (uint32_t b = tid; b < nbk; b += T) {
+        float v[32];
+        const uint8_t* src = bfrag + (size_t)b * GEMV_BFRAG_BYTES;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 t4 = *reinterpret_cast<const float4*>(src + q * 16);
+            v[4 * q] = t4.x;
+            v[4 * q + 1] = t4.y;
+            v[4 * q + 2] = t4.z;
+            v[4 * q + 3] = t4.w;
+        }
+        float m = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) m = fmaxf(m, fabsf(v[k]));
+        // Grid 2^-sh with sh = 22 - e, m = f 2^e (f in [0.5, 1)): for a
+        // normal m, e = E - 126 with E its biased exponent field.  A
+        // subnormal m uses E = 1 (a coarser grid, still |X| <= 2^22), an
+        // all-zero block any E.  v 2^sh is formed as two exact
+        // power-of-two products (sh spans -106..147); an intermediate
+        // can only lose bits when the final value rounds to 0 anyway.
+        const int E = m > 0.0f ? max((int)(__float_as_uint(m) >> 23), 1) : 126;
+        const int sh = 148 - E;
+        int X[32];
+        if (sh <= 127) {  // one exact product (every block but the tiniest)
+            const float pw = __int_as_float((sh + 127) << 23);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) X[k] = __float2int_rn(__fmul_rn(v[k], pw));
+        } else {
+            const int s1 = sh >> 1, s2 = sh - s1;
+            const float p1 = __int_as_float((s1 + 127) << 23), p2 = __int_as_float((s2 + 127) << 23);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) X[k] = __float2int_rn(__fmul_rn(__fmul_rn(v[k], p1), p2));
+        }
+        // Balanced limbs X = 65536 a + 256 b + c, b and c in [-128, 128):
+        // c = X mod 256 (as a signed byte), b = floor((X + 128) / 256) mod
+        // 256, a = floor((X + 32896) / 65536), i.e. byte 0 of X, byte 1 of
+        // X + 0x80 and byte 2 of X + 0x8080; gathered four elements at a
+        // time with byte permutes.  B fragment of lane L = g*4 + t (g < 3 =
+        // limb): word 0 = limb g of k 4t..4t+3, word 1 = limb g of k
+        // 16+4t..16+4t+3, so quad q (k = 4q..4q+3) is word 2*(q%4) + q/4 of
+        // the limb's 32 bytes.
+        uint32_t la[8], lb[8], lc[8];
+        int sx = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint32_t x0 = (uint32_t)X[4 * q], x1 = (uint32_t)X[4 * q + 1];
+            const uint32_t x2 = (uint32_t)X[4 * q + 2], x3 = (uint32_t)X[4 * q + 3];
+            const int w = 2 * (q % 4) + q / 4;
+            lc[w] = __byte_perm(__byte_perm(x0, x1, 0x0040), __byte_perm(x2, x3, 0x0040), 0x5410);
+            lb[w] = __byte_perm(__byte_perm(x0 + 0x80u, x1 + 0x80u, 0x0051),
+                                __byte_perm(x2 + 0x80u, x3 + 0x80u, 0x0051), 0x5410);
+            la[w] = __byte_perm(__byte_perm(x0 + 0x8080u, x1 + 0x8080u, 0x0062),
+                                __byte_perm(x2 + 0x8080u, x3 + 0x8080u, 0x0062), 0x5410);
+            sx += (X[4 * q] + X[4 * q + 1]) + (X[4 * q + 2] + X[4 * q + 3]);
+        }
+        uint4* bf = reinterpret_cast<uint4*>(bfrag + (size_t)b * GEMV_BFRAG_BYTES);
+        bf[0] = make_uint4(la[0], la[1], la[2], la[3]);
+        bf[1] = make_uint4(la[4], la[5], la[6], la[7]);
+        bf[2] = make_uint4(lb[0], lb[1], lb[2], lb[3]);
+        bf[3] = make_uint4(lb[4], lb[5], lb[6], lb[7]);
+        bf[4] = make_uint4(lc[0], lc[1], lc[2], lc[3]);
+        bf[5] = make_uint4(lc[4], lc[5], lc[6], lc[7]);
+        bf[6] = make_uint4(0u, 0u, 0u, 0u);  // column 3 (B lanes 12..15) is zero
+        bf[7] = make_uint4(0u, 0u, 0u, 0u);
+        // 2^-sh = 2^(E-148): normal for E >= 22, else the subnormal
+        // 2^(E+1) * 2^-149.  Lane t of the D fragment: t = 0 weighs
+        // 256*D_a + D_b by 256 f; t = 1 weighs D_c by f and adds the
+        // -8*sum(X) correction; t = 2, 3 carry no limb and weigh 0.
+        const float f = __uint_as_float(E >= 22 ? (uint32_t)(E - 21) << 23 : 1u << (E + 1));
+        float4* fs = reinterpret_cast<float4*>(fsc + (size_t)b * 4);
+        fs[0] = make_float4(f * 256.0f, 0.0f, f, f * (-8.0f * (float)sx));
+        fs[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
     if (dry) return;
