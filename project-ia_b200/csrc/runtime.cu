@@ -115,6 +115,22 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
         max_nb = std::max(max_nb, mats[i]->nb);
     }
     if (grid == 0) return false;
+#ifndef QB200_WHOLE_SLAB_PCT
+#define QB200_WHOLE_SLAB_PCT 60
+#endif
+    // Whole slabs: a grid that divides the slab count gives every CTA the
+    // same whole slabs, so no slab is split across CTAs and no partial sums
+    // or tickets are needed.  Worth it while the grid still covers most
+    // SMs (measured: 96 of 148 SMs still stream these matrices at close to the
+    // full HBM rate, and the split-slab finish costs more than the idle SMs).
+    if (n == 1) {
+        const uint64_t ns = mats[0]->n_slabs;
+        for (uint64_t d = std::min<uint64_t>(grid, ns); d >= 1; --d) {
+            if (ns % d) continue;
+            if (d * 100 >= (uint64_t)device_sms() * QB200_WHOLE_SLAB_PCT) grid = d;
+            break;
+        }
+    }
     cp = ChainPlan{};
     cp.n = n;
     cp.grid = (uint32_t)grid;
