@@ -60,7 +60,7 @@ struct AttnArgs {
     float* out;              // [n_heads][hd]
     const StepParams* step;
     uint32_t n_heads, n_kv_heads, max_seq;
-    uint32_t chunk_alloc;    // >= ceil(max_seq / CS), a multiple of 4: scores per query head
+    uint32_t chunk_alloc;    // >= the longest chunk (whole stages of 16 KB / (4 hd) rows): scores per query head
     uint32_t slots;          // ring depth (2..ATT_MAX_SLOTS)
     float scale;             // 1/sqrtf(hd), computed on the host like upstream
     unsigned long long* trace;  // step-trace slot (null: off)
@@ -162,8 +162,10 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     // Step scalars come from the previous graph replay or a host copy, both
     // complete before this grid starts.
     const uint32_t valid = a.step->valid, N = a.step->n_row, cur = a.step->pos;
-    const uint32_t chunk = (valid + CS - 1) / CS;
-    const uint32_t p0 = min(r * chunk, valid), p1 = min(p0 + chunk, valid);
+    // CTA r takes whole ring stages [n_st r / CS, n_st (r+1) / CS) of the
+    // valid rows, so only the last stage of the sequence is a partial box
+    const uint32_t n_st = (valid + SP - 1) / SP;
+    const uint32_t p0 = min(n_st * r / CS * SP, valid), p1 = min(n_st * (r + 1) / CS * SP, valid);
     const int plane = (int)(a.layer * a.n_kv_heads + h);
 
     if (warp == NW) {

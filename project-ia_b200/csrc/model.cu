@@ -281,7 +281,9 @@ q_error_code plan_attention(DevState* s) {
             cudaGetLastError();
             continue;
         }
-        const uint32_t ca = ((c.max_seq_len + cs - 1) / cs + 3) / 4 * 4;
+        // chunks are whole ring stages of sp rows (the kernel's split)
+        const uint32_t sp = ATT_STAGE_BYTES / (s->hd * 4);
+        const uint32_t ca = ((c.max_seq_len + sp - 1) / sp + cs - 1) / cs * sp;
         for (uint32_t slots = ATT_MAX_SLOTS; slots >= 2; --slots) {
             const size_t smem = attn_smem_bytes(G, s->hd, ca, slots);
             if (smem > limit) continue;
