@@ -117,16 +117,17 @@ q_error_code q_b200_gemv_f32(const float* d_w, uint32_t M, uint32_t K, const flo
     if (!d_w || !d_x || !d_y) return Q_ERR_INVALID_ARG;
     if (M == 0 || K == 0 || K % 4) return Q_ERR_INVALID_SIZE;
     if (((uintptr_t)d_w & 15) || ((uintptr_t)d_x & 15)) return Q_ERR_MISALIGNED;
-    if ((size_t)K * 4 > 160 * 1024) return Q_ERR_INVALID_SIZE;
     HeadArgs h{};
+    h.slots = head_slots(K);
+    if (!h.slots) return Q_ERR_INVALID_SIZE;
     h.w = d_w;
     h.x = d_x;
     h.rows = M;
     h.K = K;
     h.logits = d_y;
-    Q_CUDA(ensure_smem_attr((const void*)lm_head_kernel, 160 * 1024));
-    const uint32_t grid = std::max<uint32_t>(1, std::min<uint32_t>(2 * device_sms(), (M + 15) / 16));
-    Q_CUDA(launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), (size_t)K * 4,
+    Q_CUDA(ensure_smem_attr((const void*)lm_head_kernel, 227 * 1024));
+    const uint32_t grid = std::max<uint32_t>(1, std::min<uint32_t>(device_sms(), M));
+    Q_CUDA(launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), head_smem_bytes(K, h.slots),
                      (cudaStream_t)stream, false, h));
     return Q_OK;
 }

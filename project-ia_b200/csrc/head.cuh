@@ -5,8 +5,8 @@
 // q_matmul_f32_avx2 against the transposed FP32 output view) and the greedy
 // branch of q_sample_token (src/main.c:870-881: the first index of the
 // maximum).  The head streams W_out [V][D] fp32 (2.1 GB at the 8B shape)
-// with 16-byte non-allocating loads, x normalised once per CTA into shared
-// memory, packed FFMA2 accumulation, and folds the argmax into a 64-bit
+// through a shared-memory ring by bulk copies, x normalised once per CTA
+// into shared memory, packed FFMA2 accumulation, and folds the argmax into a 64-bit
 // atomicMax over (order-preserving float bits, ~index) so ties resolve to
 // the lowest index exactly like upstream's strict '>' scan.
 #pragma once
@@ -16,7 +16,12 @@
 
 namespace qb200 {
 
-static constexpr int HEAD_THREADS = 256;
+static constexpr int HEAD_CWARPS = 8;                            // consumer warps
+static constexpr int HEAD_THREADS = HEAD_CWARPS * 32 + 32;         // + producer warp
+static constexpr uint32_t HEAD_STAGE_BYTES = 64 * 1024;            // one ring slot
+static constexpr uint32_t HEAD_MAX_SLOTS = 3;
+static constexpr uint32_t HEAD_MAX_PARTS = 8;                      // warps sharing one row
+static constexpr uint32_t HEAD_MAX_ROWS_PER_STAGE = 32;
 
 struct HeadArgs {
     const float* w;            // [rows][K] fp32
@@ -25,10 +30,25 @@ struct HeadArgs {
     float eps;
     uint32_t rows, K;
     uint32_t row_base;         // global index of row 0 (vocab split)
+    uint32_t slots;            // ring depth (2..HEAD_MAX_SLOTS)
     float* logits;             // [rows]
     unsigned long long* best;  // argmax key (null: none)
     unsigned long long* trace; // step-trace slot (null: off)
 };
+
+// Shared memory: ring[slots][HEAD_STAGE_BYTES] | x[K] fp32.
+__host__ __device__ inline size_t head_smem_bytes(uint32_t K, uint32_t slots) {
+    return (size_t)slots * HEAD_STAGE_BYTES + (size_t)K * 4;
+}
+
+// Ring depth for K: as many 64 KB slots (2..3) as fit beside x in the
+// 220 KB budget; 0 when K is out of range (K % 4, K * 4 > one slot).
+inline uint32_t head_slots(uint32_t K) {
+    if (K == 0 || K % 4 || (size_t)K * 4 > HEAD_STAGE_BYTES) return 0;
+    for (uint32_t sl = HEAD_MAX_SLOTS; sl >= 2; --sl)
+        if (head_smem_bytes(K, sl) <= 220 * 1024) return sl;
+    return 0;
+}
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
     uint32_t b = __float_as_uint(v);
@@ -36,90 +56,139 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
     return ((unsigned long long)b << 32) | (0xFFFFFFFFu - idx);
 }
 
-__global__ void __launch_bounds__(HEAD_THREADS) lm_head_kernel(const HeadArgs a) {
-    extern __shared__ __align__(16) float xs[];  // [K]
-    __shared__ float part[HEAD_THREADS / 32];
-    __shared__ unsigned long long wbest[HEAD_THREADS / 32];
-    if (threadIdx.x == 0) trace_mark(a.trace, 0);
-    pdl_trigger();
-    pdl_wait();
-    if (threadIdx.x == 0) trace_mark(a.trace, 1);
+// One CTA per SM over a contiguous range of rows.  The producer warp
+// streams the range through the ring in stages of whole rows (one 1-D bulk
+// copy per stage, this GPU's own memory, no multicast), starting before the
+// programmatic-dependency wait since the weights do not depend on the
+// previous kernel.  The consumer warps split each stage into (row, part)
+// items — a row in P = 8 / rows-per-stage parts — take items round-robin,
+// and leave one partial per item in shared memory; the row's logit is the
+// sum of its P partials in part order.  Requires K * 4 <= HEAD_STAGE_BYTES
+// and K % 4 == 0 (host-checked).
+__global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs a) {
+    extern __shared__ __align__(128) uint8_t hsm[];
+    constexpr uint32_t T = HEAD_CWARPS * 32;
+    __shared__ __align__(8) uint64_t full[HEAD_MAX_SLOTS], empty[HEAD_MAX_SLOTS];
+    __shared__ float part[HEAD_CWARPS];
+    __shared__ float red[HEAD_MAX_ROWS_PER_STAGE > HEAD_MAX_PARTS ? HEAD_MAX_ROWS_PER_STAGE : HEAD_MAX_PARTS];  // [row in stage][part]
+    __shared__ unsigned long long wbest[HEAD_CWARPS];
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t K = a.K, rb = K * 4, SR = min(HEAD_MAX_ROWS_PER_STAGE, HEAD_STAGE_BYTES / rb);  // rows per stage
+    const uint32_t P = SR >= HEAD_CWARPS ? 1u : HEAD_CWARPS / SR;      // parts per row
+    const uint32_t r0 = (uint32_t)((uint64_t)a.rows * blockIdx.x / gridDim.x);
+    const uint32_t r1 = (uint32_t)((uint64_t)a.rows * (blockIdx.x + 1) / gridDim.x);
+    float* xs = reinterpret_cast<float*>(hsm + (size_t)a.slots * HEAD_STAGE_BYTES);
+    if (tid == 0) {
+        trace_mark(a.trace, 0);
+        for (uint32_t s = 0; s < a.slots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], HEAD_CWARPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == HEAD_CWARPS) {
+        // ---- producer ---------------------------------------------------------------
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            uint32_t s = 0, ph = 0, k = 0;
+            for (uint32_t row = r0; row < r1; row += SR, ++k) {
+                if (k >= a.slots && !mbar_wait(&empty[s], ph ^ 1, QDEV_WAIT_EMPTY_TIMEOUT)) break;
+                const uint32_t bytes = min(SR, r1 - row) * rb;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(hsm + (size_t)s * HEAD_STAGE_BYTES, a.w + (size_t)row * K, bytes, &full[s], pol);
+                if (++s == a.slots) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+        }
+        pdl_wait();  // every thread waits: the grid ends after its predecessor
+        return;
+    }
+
+    // ---- consumers: normalised x into shared memory ------------------------------------
+    pdl_wait();
+    if (tid == 0) trace_mark(a.trace, 1);
     float r = 1.0f;
     if (a.norm_w) {
         float ss = 0.0f;
-        for (uint32_t i = tid; i < a.K; i += HEAD_THREADS) ss = __fmaf_rn(a.x[i], a.x[i], ss);
+        for (uint32_t i = tid; i < K; i += T) ss = __fmaf_rn(a.x[i], a.x[i], ss);
         ss = warp_sum(ss);
         if (lane == 0) part[warp] = ss;
-        __syncthreads();
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
         float tot = 0.0f;
-        for (int i = 0; i < HEAD_THREADS / 32; ++i) tot += part[i];
-        float me = __fadd_rn(__fdiv_rn(tot, (float)a.K), a.eps);
-        float r0 = __fdiv_rn(1.0f, __fsqrt_rn(me));
-        float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0, r0)));
-        r = __fmul_rn(__fmul_rn(r0, tm), 0.5f);
+        for (int i = 0; i < HEAD_CWARPS; ++i) tot += part[i];
+        float me = __fadd_rn(__fdiv_rn(tot, (float)K), a.eps);
+        float r0f = __fdiv_rn(1.0f, __fsqrt_rn(me));
+        float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0f, r0f)));
+        r = __fmul_rn(__fmul_rn(r0f, tm), 0.5f);
     }
-    for (uint32_t i = tid; i < a.K; i += HEAD_THREADS)
-        xs[i] = a.norm_w ? __fmul_rn(__fmul_rn(a.x[i], r), a.norm_w[i]) : a.x[i];
-    __syncthreads();
+    for (uint32_t i = tid; i < K; i += T) xs[i] = a.norm_w ? __fmul_rn(__fmul_rn(a.x[i], r), a.norm_w[i]) : a.x[i];
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
 
-    const uint32_t nw = gridDim.x * (HEAD_THREADS / 32);
-    const uint32_t gw = blockIdx.x * (HEAD_THREADS / 32) + warp;
-    const uint32_t n4 = a.K / 4;
+    // ---- consumers: stages ----------------------------------------------------------
+    const uint32_t n4 = K / 4, pl4 = (n4 + P - 1) / P;  // float4s per part
     const float4* x4 = reinterpret_cast<const float4*>(xs);
     unsigned long long best = 0ull;
-    for (uint32_t row = gw * 2; row < a.rows; row += nw * 2) {
-        const bool two = row + 1 < a.rows;
-        const float4* w0 = reinterpret_cast<const float4*>(a.w + (size_t)row * a.K);
-        const float4* w1 = reinterpret_cast<const float4*>(a.w + (size_t)(two ? row + 1 : row) * a.K);
-        float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-        float2 acc2 = make_float2(0.f, 0.f), acc3 = make_float2(0.f, 0.f);
-        uint32_t i = lane;
-        for (; i + 32 < n4; i += 64) {
-            const float4 a0 = ldg_stream_f4(w0 + i), a1 = ldg_stream_f4(w0 + i + 32);
-            const float4 b0 = ldg_stream_f4(w1 + i), b1 = ldg_stream_f4(w1 + i + 32);
-            const float4 xa = x4[i], xb = x4[i + 32];
-            acc0 = __ffma2_rn(make_float2(a0.x, a0.y), make_float2(xa.x, xa.y), acc0);
-            acc0 = __ffma2_rn(make_float2(a0.z, a0.w), make_float2(xa.z, xa.w), acc0);
-            acc1 = __ffma2_rn(make_float2(a1.x, a1.y), make_float2(xb.x, xb.y), acc1);
-            acc1 = __ffma2_rn(make_float2(a1.z, a1.w), make_float2(xb.z, xb.w), acc1);
-            acc2 = __ffma2_rn(make_float2(b0.x, b0.y), make_float2(xa.x, xa.y), acc2);
-            acc2 = __ffma2_rn(make_float2(b0.z, b0.w), make_float2(xa.z, xa.w), acc2);
-            acc3 = __ffma2_rn(make_float2(b1.x, b1.y), make_float2(xb.x, xb.y), acc3);
-            acc3 = __ffma2_rn(make_float2(b1.z, b1.w), make_float2(xb.z, xb.w), acc3);
-        }
-        for (; i < n4; i += 32) {
-            const float4 a0 = ldg_stream_f4(w0 + i), b0 = ldg_stream_f4(w1 + i);
-            const float4 xa = x4[i];
-            acc0 = __ffma2_rn(make_float2(a0.x, a0.y), make_float2(xa.x, xa.y), acc0);
-            acc0 = __ffma2_rn(make_float2(a0.z, a0.w), make_float2(xa.z, xa.w), acc0);
-            acc2 = __ffma2_rn(make_float2(b0.x, b0.y), make_float2(xa.x, xa.y), acc2);
-            acc2 = __ffma2_rn(make_float2(b0.z, b0.w), make_float2(xa.z, xa.w), acc2);
-        }
-        float d0 = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-        float d1 = (acc2.x + acc2.y) + (acc3.x + acc3.y);
-        d0 = warp_sum(d0);
-        d1 = warp_sum(d1);
-        if (lane == 0) {
-            a.logits[row] = d0;
-            unsigned long long k0 = argmax_key(d0, a.row_base + row);
-            best = k0 > best ? k0 : best;
-            if (two) {
-                a.logits[row + 1] = d1;
-                unsigned long long k1 = argmax_key(d1, a.row_base + row + 1);
-                best = k1 > best ? k1 : best;
+    uint32_t s = 0, ph = 0;
+    for (uint32_t row = r0; row < r1; row += SR) {
+        const uint32_t nr = min(SR, r1 - row);
+        mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
+        const float4* st4 = reinterpret_cast<const float4*>(hsm + (size_t)s * HEAD_STAGE_BYTES);
+        for (uint32_t it = warp; it < nr * P; it += HEAD_CWARPS) {
+            const uint32_t rr = it / P, p = it % P;
+            const uint32_t b = p * pl4, e = min(n4, b + pl4);
+            const float4* wr = st4 + (size_t)rr * n4;
+            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+            uint32_t i = b + lane;
+            for (; i + 32 < e; i += 64) {
+                const float4 w0 = wr[i], w1 = wr[i + 32], xa = x4[i], xb = x4[i + 32];
+                acc0 = __ffma2_rn(make_float2(w0.x, w0.y), make_float2(xa.x, xa.y), acc0);
+                acc0 = __ffma2_rn(make_float2(w0.z, w0.w), make_float2(xa.z, xa.w), acc0);
+                acc1 = __ffma2_rn(make_float2(w1.x, w1.y), make_float2(xb.x, xb.y), acc1);
+                acc1 = __ffma2_rn(make_float2(w1.z, w1.w), make_float2(xb.z, xb.w), acc1);
             }
+            if (i < e) {
+                const float4 w0 = wr[i], xa = x4[i];
+                acc0 = __ffma2_rn(make_float2(w0.x, w0.y), make_float2(xa.x, xa.y), acc0);
+                acc0 = __ffma2_rn(make_float2(w0.z, w0.w), make_float2(xa.z, xa.w), acc0);
+            }
+            const float d = warp_sum((acc0.x + acc0.y) + (acc1.x + acc1.y));
+            if (lane == 0) red[rr * P + p] = d;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == a.slots) {
+            s = 0;
+            ph ^= 1;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        if (tid < nr) {
+            float d = 0.0f;
+            for (uint32_t p = 0; p < P; ++p) d += red[tid * P + p];
+            a.logits[row + tid] = d;
+            const unsigned long long kk = argmax_key(d, a.row_base + row + tid);
+            best = kk > best ? kk : best;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(T));  // red[] free again
     }
     if (!a.best) {
         if (tid == 0) trace_mark(a.trace, 2);
         return;
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+    }
     if (lane == 0) wbest[warp] = best;
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
     if (tid == 0) {
         unsigned long long b = 0ull;
-        for (int i = 0; i < HEAD_THREADS / 32; ++i) b = wbest[i] > b ? wbest[i] : b;
+        for (int i = 0; i < HEAD_CWARPS; ++i) b = wbest[i] > b ? wbest[i] : b;
         if (b) atomicMax(a.best, b);
         trace_mark(a.trace, 2);
     }

@@ -502,18 +502,15 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
     h.logits = s->logits;
     h.best = s->best;
     h.trace = take_slot(s);
+    h.slots = head_slots(h.K);
+    if (!h.slots) return cudaErrorInvalidValue;
     {
-        const cudaError_t e = ensure_smem_attr((const void*)lm_head_kernel, 160 * 1024);
+        const cudaError_t e = ensure_smem_attr((const void*)lm_head_kernel, 227 * 1024);
         if (e != cudaSuccess) return e;
     }
-    const uint32_t grid = std::max<uint32_t>(
-        1, std::min<uint32_t>(2 * device_sms(), (s->tp.v + 15) / 16));
-    // The grid-stride row loop gives every CTA the same work, so CTAs must
-    // spread evenly over the SMs.  Launched early under programmatic
-    // dependent launch, the scheduler would otherwise stack many CTAs on the
-    // first SMs the previous kernel frees; the shared-memory request caps
-    // residency at two CTAs per SM.
-    const size_t smem = std::max<size_t>((size_t)s->cfg.dim * 4, 96 * 1024);
+    // one CTA per SM, each a contiguous range of rows
+    const uint32_t grid = std::max<uint32_t>(1, std::min<uint32_t>(device_sms(), s->tp.v));
+    const size_t smem = head_smem_bytes(h.K, h.slots);
     cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), smem, st, true, h);
     if (e != cudaSuccess) return e;
     if (s->tp_world > 1 && s->peers_ready) {  // the argmax key over every rank's vocab rows
