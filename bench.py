@@ -134,7 +134,7 @@ class Clocks:
 
 # DRAM bytes (read + write) of one gate/up launch, from an ncu capture of
 # `bench.py --only gemv` (profiles/gemv_q4_gate_up_28672x4096.txt).
-GEMV_GU_TRAFFIC = 73_896_192
+GEMV_GU_TRAFFIC = 74_275_840
 
 
 def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
@@ -205,9 +205,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["gemv", "attention"],
-                    help="profiling runs: the gate/up GEMV alone, or a few decode steps of a "
-                         "2-layer 8B-shaped model (small vocab) over a 2048-position cache")
+    ap.add_argument("--only", choices=["gemv", "attention", "head"],
+                    help="profiling runs: the gate/up GEMV alone, a few decode steps of a "
+                         "2-layer 8B-shaped model (small vocab) over a 2048-position cache, "
+                         "or the FP32 LM-head GEMV (128256 x 4096) alone")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -245,6 +246,26 @@ def main():
     if args.only == "gemv":
         import qorus_b200 as Q
         print(json.dumps(gemv_roofline(Q, torch, 6450.9)), flush=True)
+        return
+    if args.only == "head":
+        import qorus_b200 as Q
+        M, K = CFG8B["vocab"], CFG8B["dim"]
+        g = torch.Generator(device="cuda").manual_seed(SEED)
+        w = torch.randn(M, K, device="cuda", generator=g) * 0.02
+        x = torch.randn(K, device="cuda", generator=g)
+        y = torch.empty(M, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        n = max(4, args.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(n):
+            if i == 2:
+                e0.record()
+            Q.check(Q.lib.q_b200_gemv_f32(w.data_ptr(), M, K, x.data_ptr(), y.data_ptr(), s), "gemv_f32")
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (n - 2)
+        print(json.dumps({"only": "head", "launches": n, "us_per_launch": round(us, 1),
+                          "gbs": round(M * K * 4 / (us * 1e-6) / 1e9, 1)}), flush=True)
         return
     if args.only == "attention":
         import qorus_b200 as Q
@@ -328,6 +349,23 @@ def main():
         e2e_s = float(t.item())
     e2e = args.steps / e2e_s
 
+    # in-graph kernel times of one traced step (outside the timed region):
+    # gate/up GEMV (the roofline kernel) and the LM head, with their bytes
+    in_graph = None
+    if world == 1:
+        st = m.profile_step(int(tok[0]), pos + args.steps).astype(np.int64)
+        L = CFG8B["layers"]
+        if len(st) == 5 * L + 2:
+            run = [int(c - max(b, st[i - 1, 2] if i else a)) for i, (a, b, c) in enumerate(st)]
+            gu = [run[3 + 5 * l] for l in range(L)]
+            gu_us = sum(gu) / len(gu) / 1e3
+            head_us = run[-2] / 1e3
+            gu_bytes = 2 * CFG8B["hidden"] * CFG8B["dim"] * 5 // 8
+            head_bytes = CFG8B["vocab"] * CFG8B["dim"] * 4
+            in_graph = {"source": "q_b200_profile_step: %globaltimer stamps of one decode step",
+                        "gate_up_us": round(gu_us, 2), "gate_up_gbs": round(gu_bytes / (gu_us * 1e-6) / 1e9, 1),
+                        "lm_head_us": round(head_us, 1), "lm_head_gbs": round(head_bytes / (head_us * 1e-6) / 1e9, 1),
+                        "step_us": round((st[-1, 2] - st[0, 0]) / 1e3, 1)}
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("hbm_gbs", 6650.0))
     roof = gemv_roofline(Q, torch, peak)
@@ -358,6 +396,7 @@ def main():
                        "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (7 GB streamed per token)"},
             "roofline": roof,
+            "in_graph": in_graph,
             # the token's bytes over all ranks' HBM (each rank streams its shard)
             "step_roofline": {"bytes_per_token": step_bytes, "achieved": round(step_gbs, 1),
                               "peak": round(peak * world, 1), "unit": "GB/s",
