@@ -65,7 +65,7 @@ extern "C" q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M,
     NoAllocDevice& d = g_noalloc_dev[dev];
     std::call_once(d.once, [&d] {
         d.err = cudaGetSymbolAddress(&d.scratch, g_noalloc_scratch);
-        if (d.err == cudaSuccess) d.err = ensure_smem_attr((const void*)gemv_q4_kernel, 227 * 1024);
+        if (d.err == cudaSuccess) d.err = ensure_smem_attr((const void*)gemv_q4_kernel<false>, 227 * 1024);
     });
     Q_CUDA(d.err);
     GemvArgs a{};

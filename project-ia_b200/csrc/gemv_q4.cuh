@@ -98,11 +98,32 @@ struct GemvArgs {
     uint32_t hd, q_rows, kv_rows, max_seq;
 };
 
+// Tensor-parallel exchange fused into the GEMVs (peer memory).  Each
+// rank's exchange area (at byte tp_off of every rank's buffer) holds
+// recv[2][W][tp_slice] fp32 | flag[2][W][GEMV_TP_MAX_CTAS] | ticket[2] u32.
+//   tp_send: the epilogue stores the finished rows (plus the residual on
+//   the rank whose epilogue adds it) into recv[tp_par][rank][row] of every
+//   rank instead of y, and CTA c, once its rows are stored, sets
+//   flag[tp_par][rank][c] = 1 on every rank (release, system scope; one
+//   word per CTA, so no two CTAs write the same remote word);
+//   tp_recv: every CTA's prologue waits (bounded) for the tp_expect flags
+//   of parity tp_par (W ranks x the sending grid); the last CTA past the
+//   wait (local ticket) clears them; each CTA then takes the input as the sum of the W slots in rank order (the
+//   bits a one-shot all-reduce would give).  A flag is set again only for
+//   the next exchange of the same parity, which needs this rank's next
+//   send, which runs after this grid.
+struct GemvTp {
+    uint8_t* tp_base[8];       // every rank's exchange buffer, mapped here
+    uint32_t tp_off, tp_slice, tp_world, tp_rank;
+    uint32_t tp_send, tp_recv, tp_par, tp_expect;
+};
+
 // A chain of up to GEMV_MAX_PHASES GEMVs run by one persistent grid: phase
 // p + 1 reads what phase p wrote, so consumers pass a grid barrier between
 // phases, while the producer warps stream the next matrices' weights
 // straight through it (weights never depend on activations).
 static constexpr int GEMV_MAX_PHASES = 4;
+static constexpr uint32_t GEMV_TP_MAX_CTAS = 256;  // flag words per (parity, rank)
 struct GemvChain {
     GemvArgs ph[GEMV_MAX_PHASES];
     uint32_t n_phases;
@@ -112,6 +133,7 @@ struct GemvChain {
     uint32_t max_nb;            // largest nb of the phases (input-fragment table size)
     uint32_t* bar;              // n_phases counters, zero between launches (n_phases > 1)
     unsigned long long* trace;  // step-trace slot (null: off)
+    GemvTp tp;                  // single-phase launches of gemv_q4_kernel<true> only
 };
 
 // Shared memory: ring | bfrag[max_nb][144] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
@@ -155,10 +177,20 @@ __device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uin
 
 // Epilogue for lanes 0..15 of one warp holding the 16 finished rows of slab j
 // (lane = row within the slab).  Pairs use the odd lane's value via shuffle.
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, uint32_t j, uint32_t lane, float v) {
+template <bool TP>
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const GemvTp& tpa, uint32_t j, uint32_t lane,
+                                              float v) {
     const float vn = __shfl_down_sync(0xffffffffu, v, 1);
     const uint32_t row = j * GEMV_SLAB_ROWS + lane;
     if (row >= a.M) return;
+    if constexpr (TP) {
+        if (tpa.tp_send) {  // EPI_STORE / EPI_RESID rows to every rank's receive slot
+            const float o = a.epi == EPI_RESID ? __fadd_rn(__ldcg(&a.resid[row]), v) : v;
+            const size_t at = tpa.tp_off + (((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * tpa.tp_slice + row) * 4;
+            for (uint32_t r = 0; r < tpa.tp_world; ++r) *reinterpret_cast<float*>(tpa.tp_base[r] + at) = o;
+            return;
+        }
+    }
     if (a.epi == EPI_STORE) {
         a.y[row] = v;
     } else if (a.epi == EPI_RESID) {
@@ -253,7 +285,7 @@ __device__ inline PhaseRange phase_range(uint32_t n_slabs, uint32_t nb, uint32_t
 // One GEMV (chain phase) for this CTA's range: input prologue, main loop over
 // the ring (slot s / parity ph carried across phases), slab reductions,
 // split-slab finish and epilogue.  Consumer threads only (T of them).
-template <uint32_t NW>
+template <uint32_t NW, bool TP>
 __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c, uint8_t* smem,
                                            uint8_t* bfrag, float2* fsc, float* red, uint64_t* full,
                                            uint64_t* empty, float* rms_part, uint32_t& s,
@@ -288,12 +320,69 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     const float4* g4 = reinterpret_cast<const float4*>(a.norm_w);
     constexpr int NR = 8;
     float r_norm = 1.0f;
+    const float4* rx4 = nullptr;  // tensor-parallel receive slots of this exchange, [W][tp_slice]
+    const GemvTp& tpa = c.tp;
+    if (TP && tpa.tp_recv) {
+        uint8_t* mine = tpa.tp_base[tpa.tp_rank] + tpa.tp_off;
+        uint32_t* flag = reinterpret_cast<uint32_t*>(mine + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4) +
+                         (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS;
+        rx4 = reinterpret_cast<const float4*>(mine + (size_t)tpa.tp_par * tpa.tp_world * tpa.tp_slice * 4);
+        // flags of sending CTAs 0..tp_expect/W-1 of every rank; every CTA
+        // of this grid waits for all of them, the last one past the wait
+        // (local ticket) clears them
+        uint32_t* ticket = flag - (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS +
+                           (size_t)2 * tpa.tp_world * GEMV_TP_MAX_CTAS + tpa.tp_par;
+        const uint32_t per = tpa.tp_expect / tpa.tp_world;
+        const unsigned long long t0 = gtimer();
+        for (uint32_t i = tid; i < tpa.tp_expect; i += T) {
+            const uint32_t* f = flag + (size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per;
+            while (ld_acquire_sys(f) == 0u) {
+                if (gtimer() - t0 > Q_WAIT_NS) {
+                    qdev_fail(QDEV_PEER_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __shared__ uint32_t s_tp_last;
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        if (tid == 0) s_tp_last = atomicAdd(ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        if (s_tp_last) {
+            // no rank sets these again before this grid has finished
+            for (uint32_t i = tid; i < tpa.tp_expect; i += T) flag[(size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per] = 0u;
+            if (tid == 0) *ticket = 0u;
+        }
+    }
     for (uint32_t base = 0; base < n4; base += T * NR) {
         float4 xv[NR];
+        if (!TP || !rx4) {
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
-            const uint32_t i = base + tid + T * r;
-            xv[r] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < NR; ++r) {
+                const uint32_t i = base + tid + T * r;
+                xv[r] = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        } else {
+            // the W received slots, added in rank order as the one-shot
+            // all-reduce adds them
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const uint32_t i = base + tid + T * r;
+                xv[r] = i < n4 ? __ldcg(rx4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            for (uint32_t q = 1; q < tpa.tp_world; ++q) {
+                const float4* src = rx4 + (size_t)q * (tpa.tp_slice / 4);
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    const uint32_t i = base + tid + T * r;
+                    if (i < n4) {
+                        const float4 t4 = __ldcg(src + i);
+                        xv[r].x += t4.x;
+                        xv[r].y += t4.y;
+                        xv[r].z += t4.z;
+                        xv[r].w += t4.w;
+                    }
+                }
+            }
         }
 #ifdef QB200_CHAIN_TS
         if (tid == 0 && base == 0 && pidx == 0 && !dry) {
@@ -504,7 +593,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
                     finish = true;
                 }
             }
-            if (finish) gemv_epilogue(a, j, lane, v);
+            if (finish) gemv_epilogue<TP>(a, c.tp, j, lane, v);
         }
         j_batch += cnt;
         jl = 0;
@@ -587,9 +676,19 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     CHAIN_TS(tsb + 2);
     if (jl) reduce_batch(jl);
     asm volatile("bar.sync 1, %0;" ::"r"(T));  // tables and red[] free for the next phase
+    if (TP && tpa.tp_send && tid < tpa.tp_world) {
+        // every row this CTA finished is stored (bar.sync above): publish to
+        // rank tid
+        __threadfence_system();
+        uint32_t* f = reinterpret_cast<uint32_t*>(tpa.tp_base[tid] + tpa.tp_off + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4);
+        st_release_sys(f + ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * GEMV_TP_MAX_CTAS + cta, 1u);
+    }
     CHAIN_TS(tsb + 3);
 }
 
+// TP: the single-phase tensor-parallel form (c.tp: exchange fused into
+// the epilogue / prologue); the other instantiation carries none of it.
+template <bool TP>
 __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
     gemv_q4_kernel(const __grid_constant__ GemvChain c) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -723,7 +822,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
             if (p == 2) CHAIN_TS(19);
             asm volatile("bar.sync 1, %0;" ::"r"(T));
         }
-        gemv_phase<NW>(s_args[p], c, smem, bfrag, fsc, red, full, empty, rms_part, s, ph, p, dry, s_rng[p]);
+        gemv_phase<NW, TP>(s_args[p], c, smem, bfrag, fsc, red, full, empty, rms_part, s, ph, p, dry, s_rng[p]);
         if (dry) continue;
         if (p == 1) CHAIN_TS(18);
         if (p + 1 < P && tid == 0) {

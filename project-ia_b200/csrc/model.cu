@@ -442,6 +442,32 @@ static cudaError_t allreduce_sum(DevState* s, float* buf, size_t count, cudaStre
     return nccl_status(n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, s->comm, st));
 }
 
+// Tensor-parallel exchange fused into the GEMVs (peer memory only; set
+// QORUS_B200_TP_FUSED=0 for the separate all-reduce kernel): wo and down
+// send their rows to every rank, gate/up and the next layer's QKV receive
+// and sum them.  Parity 0 carries wo's exchange, parity 1 down's.
+static bool tp_fused(const DevState* s) {
+    if (s->tp_world < 2 || !s->peers_ready) return false;
+    if (s->cp_wo.grid > GEMV_TP_MAX_CTAS || s->cp_down.grid > GEMV_TP_MAX_CTAS) return false;
+    const char* e = getenv("QORUS_B200_TP_FUSED");
+    return !(e && e[0] == '0');
+}
+static void tp_fuse(const DevState* s, GemvArgs& g, GemvTp& t, bool send, uint32_t par, uint32_t expect) {
+    for (uint32_t r = 0; r < s->tp_world; ++r) t.tp_base[r] = s->peers.base[r];
+    t.tp_off = (uint32_t)tp_fused_offset(s->tp_world, s->peer_slice);
+    t.tp_slice = s->peer_slice;
+    t.tp_world = s->tp_world;
+    t.tp_rank = s->tp_rank;
+    t.tp_par = par;
+    if (send) {
+        t.tp_send = 1;
+    } else {
+        t.tp_recv = 1;
+        t.tp_expect = expect;
+        g.x_copy = s->x;  // CTA 0 stores the summed input: the residual stream
+    }
+}
+
 static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
     const q_llama_config& c = s->cfg;
     const uint32_t D = c.dim;
@@ -473,6 +499,15 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         ph[2].epi = residual_epi(s);
         const bool more = l + 1 < c.n_layers;
         if (more) ph[3] = qkv_args(s, kv, l + 1);
+        GemvTp tps[4] = {};
+        if (tp_fused(s)) {
+            tp_fuse(s, ph[0], tps[0], true, 0, 0);
+            tp_fuse(s, ph[1], tps[1], false, 0, s->cp_wo.grid * s->tp_world);
+            if (more) {  // the last layer's down feeds the head through the all-reduce kernel
+                tp_fuse(s, ph[2], tps[2], true, 1, 0);
+                tp_fuse(s, ph[3], tps[3], false, 1, s->cp_down.grid * s->tp_world);
+            }
+        }
         const GemvPlan* mats[4] = {&s->p_wo, &s->p_gu, &s->p_down, &s->p_qkv};
         if (s->chain_phases > 1) {
             e = launch_chain(more ? s->cp_mid : s->cp_last, mats, ph, s->gemv_scratch,
@@ -481,9 +516,10 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
             // one GEMV per launch, chained by programmatic dependent launch
             const ChainPlan* one[4] = {&s->cp_wo, &s->cp_gu, &s->cp_down, &s->cp_first};
             for (uint32_t i = 0; i < (more ? 4u : 3u) && e == cudaSuccess; ++i) {
-                e = launch_chain(*one[i], &mats[i], &ph[i], s->gemv_scratch, nullptr, take_slot(s), st, true);
+                e = launch_chain(*one[i], &mats[i], &ph[i], s->gemv_scratch, nullptr, take_slot(s), st, true,
+                                 &tps[i]);
                 // wo and down hold partial residual updates on a tensor-parallel rank
-                if (e == cudaSuccess && (i == 0 || i == 2)) e = allreduce_sum(s, s->x, c.dim, st);
+                if (e == cudaSuccess && (i == 0 || i == 2) && !tps[i].tp_send) e = allreduce_sum(s, s->x, c.dim, st);
             }
         }
     }

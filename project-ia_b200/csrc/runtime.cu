@@ -173,7 +173,7 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
 
 cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const GemvArgs* args,
                          void* scratch, uint32_t* bar, unsigned long long* trace, cudaStream_t s,
-                         bool pdl) {
+                         bool pdl, const GemvTp* tp) {
     GemvChain c{};
     for (uint32_t i = 0; i < cp.n; ++i) {
         GemvArgs a = args[i];
@@ -194,7 +194,11 @@ cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const
     c.bar = bar;
     c.trace = trace;
     if (cp.n > 1 && !bar) return cudaErrorInvalidValue;
-    cudaError_t e = ensure_smem_attr((const void*)gemv_q4_kernel, 227 * 1024);
+    const bool fused = tp && (tp->tp_send || tp->tp_recv);
+    if (fused && cp.n != 1) return cudaErrorInvalidValue;
+    if (fused) c.tp = *tp;
+    const void* kern = fused ? (const void*)gemv_q4_kernel<true> : (const void*)gemv_q4_kernel<false>;
+    cudaError_t e = ensure_smem_attr(kern, 227 * 1024);
     if (e != cudaSuccess) return e;
     // Phases after the first wait on the whole grid: all CTAs must be
     // resident at once (cooperative launch).
@@ -218,7 +222,8 @@ cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const
     cfg.attrs = attr;
     cfg.numAttrs = na;
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
-    return cudaLaunchKernelEx(&cfg, gemv_q4_kernel, c);
+    void* params[1] = {&c};
+    return cudaLaunchKernelExC(&cfg, kern, params);
 }
 
 bool plan_single(uint32_t M, uint32_t K, GemvPlan& p, ChainPlan& cp) {

@@ -53,14 +53,6 @@ const NcclApi* nccl() {
 
 // ---- peer-memory all-reduce kernel ----------------------------------------------
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __global__ void __launch_bounds__(512) tp_allreduce_kernel(const TpArgs a) {
     constexpr uint32_t T = 512;
