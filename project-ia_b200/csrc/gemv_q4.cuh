@@ -30,9 +30,13 @@
 // bulk copy.
 //
 // Work split.  The grid's CTAs take equal contiguous ranges of the block
-// sequence (slab-major), so every CTA streams the same bytes.  A slab cut
-// by a range boundary is finished by the last of its CTAs to arrive
+// sequence (slab-major), so every CTA streams the same bytes; the host
+// prefers a grid that divides the slab count (whole slabs per CTA).  A slab
+// cut by a range boundary is finished by the last of its CTAs to arrive
 // (per-slab ticket in global scratch), which adds the parts in CTA order.
+// Input prologue: coalesced loads staged in shared memory, then one thread
+// per 32-value block builds its limb fragment (rows padded to 144 bytes).
+// gemv_q4_kernel<true> adds the tensor-parallel exchange (GemvTp).
 // Inside a CTA a producer warp streams stages through a shared-memory ring
 // with cp.async.bulk + mbarrier; weight loads start before the programmatic
 // dependent launch wait.  Consumer warp w handles the blocks of a slab with

@@ -1,12 +1,14 @@
-// tp.cuh — tensor parallelism across the GPUs of one node: shard geometry
-// and the NCCL entry points the decode graph uses.
+// tp.cuh — tensor parallelism across the GPUs of one node: shard geometry,
+// the peer-memory exchange buffers and kernel, and the NCCL entry points the
+// decode graph uses.
 //
 // Rank r of W holds: query heads [r*nh/W, (r+1)*nh/W) and KV heads
 // [r*nkv/W, ...) (so the QKV projection and the KV cache are split by head),
 // FFN rows [r*H/W, ...) of gate and up, the matching K-slices of wo (its
 // heads' columns) and down (its FFN columns), and vocab rows
 // [r*ceil(V/W), ...) of the LM head.  wo and down produce partial residual
-// updates that an all-reduce sums; the argmax key is all-reduced with max.
+// updates that an all-reduce sums (fused into the GEMVs over peer memory
+// when it is set up, see GemvTp); the argmax key is all-reduced with max.
 // Norm gains, RoPE tables and the embedding are replicated.
 //
 // NCCL is opened at run time (dlopen of libnccl.so.2) so the library binds
