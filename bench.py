@@ -21,7 +21,15 @@ strong scaling: value is the sequence's tok/s).
 
 --impl reference times the upstream CPU implementation of the same path:
 the upstream AVX2 kernels (compiled from the upstream sources into
-oracle/_ref) composed into the same graph, all host threads.
+oracle/_ref) composed into the same graph, all host threads.  That process
+never loads the CUDA library: its model file and KV image come from
+oracle/libqgen.so (the same generator source, built on its own).
+
+The line also carries the GEMV sweep of BASELINE configs[1] (`sweep`: the
+four Llama-3-8B projection shapes, GB/s against the measured HBM peak,
+upstream's q_gemv_q4_f32_avx2 on one host thread beside each), and
+`cpu_baseline` is upstream's decode on ONE host thread (the reference has no
+threading), with the all-threads figure under cpu_baseline.threaded.
 """
 from __future__ import annotations
 
@@ -45,6 +53,12 @@ METRIC = "Llama-3-8B Q4_0 decode tok/s"
 CFG8B = dict(vocab=128256, dim=4096, hidden=14336, layers=32, heads=32, kv_heads=8)
 PREFILL = 2048
 SEED = 0
+# the workload, printed identically by both arms
+CONFIG = {"workload": "llama3-8b-q4_0 decode, batch 1, kv prefill 2048 (BASELINE configs[2])",
+          "layers": 32, "dim": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
+          "global_batch": 1, "prefill": PREFILL,
+          "l2": "inputs larger than L2 (7 GB streamed per token)"}
+SWEEP = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
 
 
 def q4_linear_bytes(c) -> int:
@@ -69,21 +83,26 @@ def model_path(max_seq: int) -> str:
     return str(d / f"qorus_llama3_8b_q4_{max_seq}_s{SEED}.qorus")
 
 
-def ensure_model(Q, max_seq: int, rank: int, barrier) -> tuple[str, object]:
-    cfg = Q.config(CFG8B["vocab"], CFG8B["dim"], CFG8B["hidden"], CFG8B["layers"],
-                   CFG8B["heads"], CFG8B["kv_heads"], max_seq)
+def ensure_model(gen, cfg, max_seq: int, rank: int, barrier) -> str:
+    """Write the seed-0 model file once.  `gen` is a library exporting the
+    synthetic-input generators: the product library in our arm, the
+    CPU-only oracle/libqgen.so (same C source) in the reference arm."""
     path = model_path(max_seq)
-    size = int(Q.lib.q_b200_model_file_size(C.byref(cfg)))
+    size = int(gen.q_b200_model_file_size(C.byref(cfg)))
     if rank == 0 and not (Path(path).exists() and Path(path).stat().st_size == size):
-        Q.write_model(path, cfg, seed=SEED, threads=0)
+        rc = gen.q_b200_write_model_file(path.encode(), C.byref(cfg), SEED, 0)
+        if rc:
+            raise RuntimeError(f"q_b200_write_model_file: {rc}")
     barrier()
-    return path, cfg
+    return path
 
 
-def kv_image(Q, cfg) -> np.ndarray:
+def kv_image(gen, cfg) -> np.ndarray:
     hd = cfg.dim // cfg.n_heads
     kv = np.zeros(cfg.n_layers * cfg.n_kv_heads * cfg.max_seq_len * 2 * hd, np.float32)
-    Q.check(Q.lib.q_b200_fill_kv_prefill(Q.ptr(kv), C.byref(cfg), PREFILL, SEED + 1, 0), "kv")
+    rc = gen.q_b200_fill_kv_prefill(kv.ctypes.data, C.byref(cfg), PREFILL, SEED + 1, 0)
+    if rc:
+        raise RuntimeError(f"q_b200_fill_kv_prefill: {rc}")
     return kv
 
 
@@ -169,7 +188,7 @@ def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
     us = e0.elapsed_time(e1) * 1e3 / iters
     bytes_launch = M * K * 5 // 8 + 4 * K + 4 * M
     achieved = bytes_launch / (us * 1e-6) / 1e9
-    return {"kernel": "gemv_q4_kernel (fused gate/up 28672x4096)", "bound": "hbm",
+    return {"kernel": "q4_slab_kernel (fused gate/up 28672x4096)", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "us_per_launch": round(us, 2),
             "bytes_per_launch": bytes_launch, "traffic": GEMV_GU_TRAFFIC,
@@ -177,8 +196,9 @@ def gemv_roofline(Q, torch, peak_gbs: float) -> dict:
             "peak_source": "of measured"}
 
 
-def cpu_reference_decode(path: str, cfg, steps: int, threads: int):
-    """Upstream AVX2 kernels (oracle/_ref) over the same model and KV image."""
+def cpu_reference_decode(path: str, cfg, steps: int, threads: int, budget_s: float = 1e9):
+    """Upstream AVX2 kernels (oracle/_ref) over the same model and KV image:
+    `steps` decode steps (fewer if they would pass budget_s of wall time)."""
     import oracle as O
     kind = "reference"
     try:
@@ -186,7 +206,7 @@ def cpu_reference_decode(path: str, cfg, steps: int, threads: int):
     except (RuntimeError, OSError):
         m = O.OracleModel(path, threads=threads)
         kind = "port"
-    m.kv[:] = kv_image(__import__("qorus_b200"), cfg)
+    m.kv[:] = kv_image(O.gen, cfg)
     tok = 1
     times = []
     for i in range(steps):
@@ -194,8 +214,70 @@ def cpu_reference_decode(path: str, cfg, steps: int, threads: int):
         lg = m.forward(np.array([tok], np.uint32), PREFILL + i)
         times.append(time.perf_counter() - t0)
         tok = int(np.argmax(lg))
+        if sum(times) * (len(times) + 1) / len(times) > budget_s:
+            break
     m.close()
     return kind, times
+
+
+def gemv_sweep(Q, torch, peak_gbs: float, host: bool) -> list:
+    """each Llama-3-8B projection shape as one Q4_0 GEMV
+    launch (q_b200_gemv_q4), CUDA events over back-to-back launches that
+    rotate over enough distinct weight sets to exceed L2 (>= 300 MB), beside
+    upstream q_gemv_q4_f32_avx2 on one host thread (1 warm-up + 5 timed
+    calls, as upstream tools/benchmark.c:22-50)."""
+    import oracle as O  # the upstream kernel, timed as the CPU baseline
+    out = []
+    s = torch.cuda.current_stream().cuda_stream
+    for M, K in SWEEP:
+        nblk = M * K // 32
+        bytes_launch = M * K * 5 // 8 + 4 * K + 4 * M
+        n_sets = max(1, -(-300_000_000 // bytes_launch))
+        n_sets = min(n_sets, 32)
+        host_w = np.zeros(nblk * 20, np.uint8)
+        packed = []
+        for i in range(n_sets):
+            Q.lib.q_b200_fill_q4(Q.ptr(host_w), nblk, SEED + 100 + i, 5, 0, 0.001, 0.01, 0)
+            src = torch.from_numpy(host_w).cuda()
+            dst = torch.empty(Q.lib.q_b200_q4_packed_bytes(M, K), dtype=torch.uint8, device="cuda")
+            torch.cuda.synchronize()
+            Q.check(Q.lib.q_b200_q4_pack(src.data_ptr(), M, K, dst.data_ptr(), None), "pack")
+            torch.cuda.synchronize()
+            packed.append(dst)
+            del src
+        x = Q.aligned_empty(K)
+        Q.lib.q_b200_fill_normal(Q.ptr(x), K, SEED, 12, 0, 0.0, 1.0, 0)
+        dx = torch.from_numpy(x.copy()).cuda()
+        dy = torch.empty(M, device="cuda")
+        iters = max(64, 4 * n_sets)
+        for i in range(8):
+            Q.check(Q.lib.q_b200_gemv_q4(packed[i % n_sets].data_ptr(), M, K, dx.data_ptr(), dy.data_ptr(), s), "gemv")
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(iters):
+            Q.lib.q_b200_gemv_q4(packed[i % n_sets].data_ptr(), M, K, dx.data_ptr(), dy.data_ptr(), s)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / iters
+        gbs = bytes_launch / (us * 1e-6) / 1e9
+        row = {"shape": f"{M}x{K}", "bytes": bytes_launch, "us": round(us, 2), "gbs": round(gbs, 1),
+               "frac": round(gbs / peak_gbs, 4), "weight_sets": n_sets}
+        del packed
+        if host:
+            y = Q.aligned_empty(M)
+            kind = O.upstream_gemv_q4(host_w, M, K, x, y)
+            ts = []
+            for _ in range(5):
+                t0 = time.perf_counter()
+                O.upstream_gemv_q4(host_w, M, K, x, y)
+                ts.append(time.perf_counter() - t0)
+            cms = 1e3 * sum(ts) / len(ts)
+            row["cpu"] = {"kind": kind, "cores": 1, "ms": round(cms, 3),
+                          "gbs": round(bytes_launch / (cms * 1e-3) / 1e9, 2)}
+            row["speedup_vs_cpu"] = round(cms * 1e3 / us, 1)
+        out.append(row)
+    return out
 
 
 def main():
@@ -215,27 +297,30 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    max_seq = PREFILL + 2 * (args.steps + args.warmup) + 64
+    max_seq = PREFILL + 2 * (args.steps + args.warmup) + 64 + 320  # + the clock soak
 
     if args.impl == "reference":
+        # CPU only: the upstream kernels; the CUDA library is never loaded here
         if rank != 0:
             return
-        import qorus_b200 as Q
-        path, cfg = ensure_model(Q, max_seq, 0, lambda: None)
+        import oracle as O
+        cfg = O.config(CFG8B["vocab"], CFG8B["dim"], CFG8B["hidden"], CFG8B["layers"],
+                       CFG8B["heads"], CFG8B["kv_heads"], max_seq)
+        path = ensure_model(O.gen, cfg, max_seq, 0, lambda: None)
         threads = os.cpu_count() or 1
-        n = max(1, min(args.steps, 16))
-        kind, times = cpu_reference_decode(path, cfg, args.warmup // 3 + n, threads)
-        times = times[args.warmup // 3:]
+        warm = 1
+        kind, times = cpu_reference_decode(path, cfg, warm + args.steps, threads, budget_s=150.0)
+        times = times[warm:]
         tps = len(times) / sum(times)
         line = {"metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "impl": "reference",
-                "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup // 3,
+                "n_gpus": args.gpus, "steps": len(times), "warmup": warm,
                 "ms_per_step": round(1e3 * sum(times) / len(times), 2), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32 (q4_0 weights)",
-                "data": "synthetic", "config": {"workload": "llama3-8b-q4_0 decode, batch 1, "
-                                                "kv prefill 2048", "prefill": PREFILL},
+                "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+                "dtype": "f32 (q4_0 weights)", "data": "synthetic", "config": CONFIG,
                 "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads,
                                  "kind": kind, "sample": f"{len(times)} decode steps of the "
-                                 "8B-shaped model at context 2049+ (every step a full token)"},
+                                 "8B-shaped model at context 2049+ (every step a full token; "
+                                 "upstream AVX2 kernels, row-parallel over all host threads)"},
                 "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -273,7 +358,7 @@ def main():
         spath = str(Path(model_path(4096)).with_name("qorus_llama3_8b_2layer_small.qorus"))
         Q.write_model(spath, small, seed=SEED, threads=0)
         ms = Q.Model(spath)
-        ms.kv_write(kv_image(Q, small))
+        ms.kv_write(kv_image(Q.lib, small))
         toks = ms.decode_loop(1, PREFILL, max(4, args.steps), sync=True)
         print(json.dumps({"only": "attention", "steps": int(len(toks))}), flush=True)
         return
@@ -287,7 +372,9 @@ def main():
             dist.barrier()
 
     import qorus_b200 as Q
-    path, cfg = ensure_model(Q, max_seq, rank, barrier)
+    cfg = Q.config(CFG8B["vocab"], CFG8B["dim"], CFG8B["hidden"], CFG8B["layers"],
+                   CFG8B["heads"], CFG8B["kv_heads"], max_seq)
+    path = ensure_model(Q.lib, cfg, max_seq, rank, barrier)
     t_load = time.perf_counter()
     tp = None
     if world > 1:
@@ -301,7 +388,7 @@ def main():
         dist.all_gather_object(allb, b)
         return allb
     m = Q.Model(path, tp=tp, tp_gather=gather if world > 1 else None)
-    kv = kv_image(Q, cfg)
+    kv = kv_image(Q.lib, cfg)
     if world > 1:  # this rank's KV heads: [L][n_kv/W][max_seq][K|V]
         sh = Q.tp_shape(cfg, rank, world)
         h0 = sh["kv0"] // (cfg.dim // cfg.n_heads)
@@ -315,11 +402,22 @@ def main():
     pos = PREFILL
     m.decode_loop(1, pos, args.warmup, sync=True)
     pos += args.warmup
-    launches0 = Q.lib.q_b200_kernel_launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
+        # the same decode steps for ~0.6 s before the timed region, untimed,
+        # so the clock sampler sees this load and not only the region's
+        # few milliseconds
+        soak = 300
+        Q.check(Q.lib.q_b200_decode_loop(C.byref(m.model), C.byref(m.ctx), 1, pos, soak, None, 0),
+                "decode_loop")
+        torch.cuda.synchronize()
+        pos += soak
+        barrier()
+        torch.cuda.synchronize()
+        launches0 = Q.lib.q_b200_kernel_launches()
+        t_pos = pos
         e0.record(stream)
         Q.check(Q.lib.q_b200_decode_loop(C.byref(m.model), C.byref(m.ctx), 1, pos, args.steps,
                                          None, 0), "decode_loop")
@@ -371,18 +469,27 @@ def main():
     roof = gemv_roofline(Q, torch, peak)
     if not peaks:
         roof["peak_source"] = "of fallback"
-    ctx_mid = PREFILL + args.warmup + args.steps // 2
+    ctx_mid = t_pos + args.steps // 2  # mean context of the timed steps
     step_bytes = token_bytes(CFG8B, ctx_mid)
     step_gbs = step_bytes / (ms * 1e-3 / args.steps) / 1e9
+
+    sweep = gemv_sweep(Q, torch, peak, host=not args.no_cpu_baseline) if world == 1 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         m.close()
-        threads = os.cpu_count() or 1
-        kind, times = cpu_reference_decode(path, cfg, 3, threads)
-        cpu = {"value": round(len(times) / sum(times), 3), "unit": "tok/s", "cores": threads,
+        # upstream as shipped: one thread (the reference has no threading)
+        kind, times = cpu_reference_decode(path, cfg, 3, 1)
+        cpu = {"value": round(len(times) / sum(times), 4), "unit": "tok/s", "cores": 1,
                "kind": kind, "sample": f"{len(times)} full decode steps of the same 8B-shaped "
-               "model and KV image (upstream AVX2 kernels, row-parallel over host threads)"}
+               "model and KV image at context 2049+ (upstream AVX2 kernels, one thread)"}
+        threads = os.cpu_count() or 1
+        kind, times = cpu_reference_decode(path, cfg, 4, threads)
+        times = times[1:]
+        cpu["threaded"] = {"value": round(len(times) / sum(times), 3), "unit": "tok/s",
+                           "cores": threads, "kind": kind,
+                           "sample": f"{len(times)} decode steps after one warm-up, the upstream "
+                           "kernels row-parallel over all host threads (the --impl reference arm's setup)"}
 
     if rank == 0:
         line = {
@@ -391,10 +498,8 @@ def main():
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
             "dtype": "f32 (q4_0 weights)", "data": "synthetic",
-            "config": {"workload": "llama3-8b-q4_0 decode, batch 1, kv prefill 2048 (BASELINE configs[2])",
-                       "layers": 32, "dim": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
-                       "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (7 GB streamed per token)"},
+            "config": CONFIG,
+            "parallelism": f"tp{world}" if world > 1 else "single",
             "roofline": roof,
             "in_graph": in_graph,
             # the token's bytes over all ranks' HBM (each rank streams its shard)
@@ -402,6 +507,7 @@ def main():
                               "peak": round(peak * world, 1), "unit": "GB/s",
                               "frac": round(step_gbs / (peak * world), 4)},
             "cpu_baseline": cpu,
+            "sweep": sweep,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 16,
                     "d2h_bytes_per_step": CFG8B["vocab"] * 4},
             "gpu_launches": int(launches),

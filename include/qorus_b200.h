@@ -148,6 +148,37 @@ q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M, uint32_t K
 q_error_code q_b200_gemv_f32(const float* d_w, uint32_t M, uint32_t K,
                              const float* d_x, float* d_y, void* stream);
 
+/* ---- device errors and bounded waits -------------------------------------
+ * No counterpart upstream (upstream's kernels run on the calling thread and
+ * cannot hang).  Every device-side wait of this library (a copy that should
+ * land in shared memory, a grid barrier, a peer rank's flag) is bounded in
+ * wall time; when one runs out the kernel records a code in a per-device
+ * status word and returns, and the upstream-API calls that synchronise
+ * (llama_forward, q_generate, q_b200_decode_loop with sync) report it as
+ * Q_ERR_INVALID_ARG with the message in q_b200_last_error().  The
+ * device-pointer entry points (q_b200_gemv_q4, q_b200_gemv_q4_noalloc, ...)
+ * are asynchronous and cannot: after synchronising their stream, read the
+ * word with q_b200_device_status. */
+
+/* Wall-time limit of every bounded device wait on the current device, in
+ * ns (default 2 s).  Applies to kernels launched after the call. */
+q_error_code q_b200_set_wait_limit_ns(uint64_t ns);
+
+/* Status word of the current device: 0 if no wait ran out since the last
+ * read, else the code of the first one (1-3 copy waits, 5 grid barrier,
+ * 6 peer flag).  Reading clears it; when it was set, this first waits for
+ * all work on the device and re-zeroes the library's ticket and barrier
+ * counters, which a wait that gave up can leave non-zero. */
+uint32_t q_b200_device_status(void);
+
+/* Self-test of the failure path: launches the fused tensor-parallel
+ * receive GEMV on the current device alone, with an exchange buffer no
+ * sender ever writes, under a wait limit of limit_ns (restored afterwards).
+ * Every CTA's flag wait runs out; *status_out receives the status word
+ * observed (6 = peer flag timeout), which is then cleared.  Returns Q_OK
+ * when the launch completed and the context is still usable. */
+q_error_code q_b200_selftest_exchange_timeout(uint64_t limit_ns, uint32_t* status_out);
+
 /* Number of kernels this library launched since load (all entry points). */
 uint64_t q_b200_kernel_launches(void);
 

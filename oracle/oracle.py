@@ -8,6 +8,9 @@ Imported by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
                            needs the upstream tree at build time; the built
                            .so travels with the repository snapshot)
   _ref/libref_forward.so   ref_forward.c over libqorus_ref.so
+  libqgen.so               the package's synthetic-input generators (qgen.c)
+                           alone, so a CPU-only process can write the model
+                           file and KV image without loading the CUDA library
 """
 from __future__ import annotations
 
@@ -62,6 +65,60 @@ if rf is not None:
 
 def p(a: np.ndarray) -> int:
     return a.ctypes.data
+
+
+# ---- synthetic inputs without the CUDA library (libqgen.so) --------------------
+
+class Config(C.Structure):
+    """q_llama_config (include/qorus_types.h)."""
+    _fields_ = [(n, C.c_uint32) for n in (
+        "vocab_size", "dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "max_seq_len")] + [
+        ("rope_freq_base", C.c_float), ("rms_norm_eps", C.c_float)]
+
+
+gen = _load("libqgen.so")
+if gen is not None:
+    gen.q_b200_model_file_size.restype, gen.q_b200_model_file_size.argtypes = _sz, [_vp]
+    gen.q_b200_write_model_file.restype = _i
+    gen.q_b200_write_model_file.argtypes = [C.c_char_p, _vp, C.c_uint64, _i]
+    gen.q_b200_fill_kv_prefill.restype, gen.q_b200_fill_kv_prefill.argtypes = _i, [_vp, _vp, _u32, C.c_uint64, _i]
+    gen.q_b200_fill_q4.restype = None
+    gen.q_b200_fill_q4.argtypes = [_vp, _sz, C.c_uint64, C.c_uint64, C.c_uint64, _f, _f, _i]
+    gen.q_b200_fill_normal.restype = None
+    gen.q_b200_fill_normal.argtypes = [_vp, _sz, C.c_uint64, C.c_uint64, C.c_uint64, _f, _f, _i]
+
+
+def config(vocab, dim, hidden, layers, heads, kv_heads, max_seq, theta=500000.0, eps=1e-5) -> Config:
+    return Config(vocab, dim, hidden, layers, heads, kv_heads, max_seq, theta, eps)
+
+
+# ---- the upstream GEMV itself (oracle/_ref), for timing beside the device -------
+
+class _QTensor(C.Structure):
+    """q_tensor (include/qorus_types.h: 64-byte aligned)."""
+    _fields_ = [("data", C.c_void_p), ("scales", C.c_void_p), ("ne", C.c_uint32 * 4),
+                ("nb", C.c_size_t * 4), ("type", C.c_int), ("name", C.c_char * 32),
+                ("_pad", C.c_uint8 * 28)]
+
+
+def upstream_gemv_q4(w_aos: np.ndarray, M: int, K: int, x: np.ndarray, y: np.ndarray) -> str:
+    """y = W x with upstream q_gemv_q4_f32_avx2 when oracle/_ref is built
+    (returns "reference"), else the restatement orc_gemv_q4 ("port").
+    x and y must be 32-byte aligned."""
+    if ref is not None:
+        t = _QTensor()
+        t.data = w_aos.ctypes.data
+        t.ne[:] = [M, K, 1, 1]
+        t.nb[:] = [K // 32 * 20, 20, 20, 20]
+        t.type = 2  # Q_Q4_0
+        rc = ref.q_gemv_q4_f32_avx2(C.byref(t), C.c_void_p(p(x)), C.c_void_p(p(y)))
+        if rc:
+            raise RuntimeError(f"q_gemv_q4_f32_avx2: {rc}")
+        return "reference"
+    orc.orc_set_threads(1)
+    if orc.orc_gemv_q4(p(w_aos), M, K, p(x), p(y)):
+        raise RuntimeError("orc_gemv_q4")
+    return "port"
 
 
 def _header(mm):

@@ -18,7 +18,12 @@
 //    rejected with Q_ERR_INVALID_SIZE (the message names both sizes);
 //  * the ticket words must be zero before a launch: device globals start
 //    zeroed and every launch leaves them zero again; the partial sums need
-//    no initial value;
+//    no initial value.  A launch whose bounded wait ran out (a device
+//    error, reported by q_b200_device_status) can leave tickets set;
+//    q_b200_device_status re-zeroes them (cudaMemset of the array, no
+//    allocation), so read it after such an error before the next call;
+//  * the address is cached per device for the life of the process: after
+//    cudaDeviceReset the process must be restarted before calling again;
 //  * one scratch per device: calls that can overlap on the device (other
 //    streams, unordered work) race on it and must be serialised by the
 //    caller.
@@ -65,7 +70,8 @@ extern "C" q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M,
     NoAllocDevice& d = g_noalloc_dev[dev];
     std::call_once(d.once, [&d] {
         d.err = cudaGetSymbolAddress(&d.scratch, g_noalloc_scratch);
-        if (d.err == cudaSuccess) d.err = ensure_smem_attr((const void*)gemv_q4_kernel<false>, 227 * 1024);
+        if (d.err == cudaSuccess) register_zero_area(d.scratch, ChainPlan::kTicketWords * 4);
+        if (d.err == cudaSuccess) d.err = ensure_smem_attr((const void*)q4_slab_kernel<false>, 227 * 1024);
     });
     Q_CUDA(d.err);
     GemvArgs a{};

@@ -266,23 +266,64 @@ void q_dequantize_q4_0_block_avx2_public(const q_block_q4_0* block, float* outpu
 
 }  // extern "C"
 
-#ifdef QB200_GEMV_PHASES
-extern "C" int q_b200_dbg_gemv_phases(void* host, size_t bytes) {
-    return (int)cudaMemcpyFromSymbol(host, qb200::g_gemv_phase, bytes);
-}
-#endif
+// ---- device status and bounded waits ---------------------------------------------
 
-#ifdef QB200_ATTN_PHASES
-extern "C" int q_b200_dbg_attn_phases(void* host, size_t bytes) {
-    return (int)cudaMemcpyFromSymbol(host, qb200::g_attn_phase, bytes);
-}
-extern "C" int q_b200_dbg_attn_stages(void* host, size_t bytes) {
-    return (int)cudaMemcpyFromSymbol(host, qb200::g_attn_stage, bytes);
-}
-#endif
+extern "C" {
 
-#ifdef QB200_CHAIN_TS
-extern "C" int q_b200_dbg_chain_ts(void* host, size_t bytes) {
-    return (int)cudaMemcpyFromSymbol(host, qb200::g_chain_ts, bytes);
+q_error_code q_b200_set_wait_limit_ns(uint64_t ns) {
+    if (ns == 0) return Q_ERR_INVALID_ARG;
+    const unsigned long long v = ns;
+    Q_CUDA(cudaMemcpyToSymbol(g_qdev_wait_ns, &v, sizeof v));
+    return Q_OK;
 }
-#endif
+
+uint32_t q_b200_device_status(void) { return take_device_status(); }
+
+q_error_code q_b200_selftest_exchange_timeout(uint64_t limit_ns, uint32_t* status_out) {
+    if (!status_out || limit_ns == 0) return Q_ERR_INVALID_ARG;
+    *status_out = 0;
+    // A single-rank receive of the fused tensor-parallel exchange whose
+    // sender never runs: every CTA's flag wait must give up after limit_ns.
+    GemvPlan p;
+    ChainPlan cp;
+    if (!plan_single(64, 256, p, cp)) return Q_ERR_INVALID_SIZE;
+    const uint32_t slice = 256;
+    const size_t xb = tp_buffer_bytes(1, slice);
+    DevBuf w, y, ex;
+    if (!w.alloc(p.packed_bytes) || !y.alloc(64 * 4) || !ex.alloc(xb)) return Q_ERR_ALLOC_FAILED;
+    void* scratch = op_gemv_scratch(cp.scratch_bytes());
+    if (!scratch) return Q_ERR_ALLOC_FAILED;
+    cudaStream_t st = op_stream();
+    Q_CUDA(cudaMemsetAsync(w.p, 0, p.packed_bytes, st));
+    Q_CUDA(cudaMemsetAsync(ex.p, 0, xb, st));
+    Q_CUDA(cudaStreamSynchronize(st));
+    if (take_device_status() != 0) return Q_ERR_INVALID_ARG;  // an earlier error is not ours
+    unsigned long long old = 0;
+    Q_CUDA(cudaMemcpyFromSymbol(&old, g_qdev_wait_ns, sizeof old));
+    const unsigned long long lim = limit_ns;
+    Q_CUDA(cudaMemcpyToSymbol(g_qdev_wait_ns, &lim, sizeof lim));
+    GemvArgs a{};
+    a.w = (const uint8_t*)w.p;
+    a.x = y.f();  // unused: the input comes from the receive slots
+    a.y = y.f();
+    a.epi = EPI_STORE;
+    GemvTp t{};
+    t.tp_base[0] = (uint8_t*)ex.p;
+    t.tp_off = (uint32_t)tp_fused_offset(1, slice);
+    t.tp_slice = slice;
+    t.tp_world = 1;
+    t.tp_rank = 0;
+    t.tp_recv = 1;
+    t.tp_par = 0;
+    t.tp_expect = 1;
+    const GemvPlan* m[1] = {&p};
+    const cudaError_t e = launch_chain(cp, m, &a, scratch, nullptr, nullptr, st, false, &t);
+    const cudaError_t e2 = cudaStreamSynchronize(st);
+    cudaMemcpyToSymbol(g_qdev_wait_ns, &old, sizeof old);
+    Q_CUDA(e);
+    Q_CUDA(e2);
+    *status_out = take_device_status();
+    return Q_OK;
+}
+
+}  // extern "C"

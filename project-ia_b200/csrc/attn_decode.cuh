@@ -108,16 +108,6 @@ __device__ __forceinline__ void st_dsmem4(float* p, uint32_t rank, float4 v) {
                  : "memory");
 }
 
-#ifdef QB200_ATTN_PHASES  // experiment builds only: per-CTA phase timestamps
-__device__ unsigned long long g_attn_phase[1024 * 8];
-__device__ unsigned long long g_attn_stage[1024 * 24];
-#define ATTN_PHASE(i) (g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + (i)] = gtimer())
-#define ATTN_STAGE(i, v) \
-    if ((i) < 24) g_attn_stage[(blockIdx.y * gridDim.x + blockIdx.x) * 24 + (i)] = (v)
-#else
-#define ATTN_PHASE(i) ((void)0)
-#define ATTN_STAGE(i, v) ((void)0)
-#endif
 
 template <int HD, int G>
 __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
@@ -150,7 +140,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
 
     if (tid == 0) {
         trace_mark(a.trace, 0);
-        ATTN_PHASE(0);
         for (uint32_t s = 0; s < SL; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NW);
@@ -188,7 +177,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
                 // the whole box arrives (rows past the chunk, or past max_seq as
                 // zeros, are loaded and ignored)
                 if (lane == 0) {
-                    ATTN_STAGE(k < 6 ? k + 6 : (k < 12 ? k + 12 : 23), gtimer());
                     mbar_arrive_expect_tx(&full[s], ATT_STAGE_BYTES);
                     tma_load_3d(ring + (size_t)s * ATT_STAGE_BYTES, &kv_map, (int)(pass * HD), (int)sp0,
                                 plane, &full[s], pol);
@@ -201,13 +189,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
             }
         }
         if (!waited) pdl_wait();  // every thread waits: the grid ends after its predecessor
-#ifdef QB200_ATTN_PHASES
-        if (lane == 0) {
-            uint32_t smid;
-            asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-            g_attn_phase[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + 7] = smid;
-        }
-#endif
         cluster_wait();
         cluster_arrive();
         cluster_wait();
@@ -217,7 +198,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     // ---- consumers -----------------------------------------------------------------
     pdl_wait();  // q is the previous kernel's output
     if (tid == 0) trace_mark(a.trace, 1);
-    if (tid == 0) ATTN_PHASE(1);
 
     uint32_t s = 0, ph = 0;
     // phase 1: scores and chunk max
@@ -238,7 +218,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
         uint32_t kst = 0;
         for (uint32_t sp0 = p0; sp0 < p1; sp0 += SP) {
             mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
-            if (tid == 0) ATTN_STAGE(kst, gtimer());
             ++kst;
             const uint32_t p = sp0 + row;
             const bool live = p < p1;
@@ -295,10 +274,8 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
             st_dsmem(&cmx[r][g], i / G, m);
         }
     }
-    if (tid == 0) ATTN_PHASE(2);
     cluster_arrive();
     cluster_wait();
-    if (tid == 0) ATTN_PHASE(3);
 
     // phase 2: global max, exponentials (upstream index rule), sums, partial P.V
     if (tid < G) {
@@ -330,7 +307,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
         uint32_t vst = 12;
         for (uint32_t sp0 = p0; sp0 < p1; sp0 += SP) {
             mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
-            if (tid == 0) ATTN_STAGE(vst, gtimer());
             ++vst;
             const uint8_t* stage = ring + (size_t)s * ATT_STAGE_BYTES;
 #pragma unroll
@@ -371,10 +347,8 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
             st_dsmem4(&pgath[r * per + o % per], o / per, acc);
         }
     }
-    if (tid == 0) ATTN_PHASE(4);
     cluster_arrive();
     cluster_wait();
-    if (tid == 0) ATTN_PHASE(5);
 
     // phase 3: this CTA's slice of the outputs, from the partials and sums
     // every CTA pushed here (summed in CTA order)
@@ -394,7 +368,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     }
     // (no shared memory of another CTA is touched after the second barrier)
     if (tid == 0) trace_mark(a.trace, 2);
-    if (tid == 0) ATTN_PHASE(6);
 }
 
 }  // namespace qb200

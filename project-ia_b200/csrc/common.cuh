@@ -4,8 +4,10 @@
 // (transaction-count barriers), cp.async.bulk (the 1-D TMA engine: global ->
 // shared copies that complete on an mbarrier), programmatic dependent launch
 // (griddepcontrol) and streaming loads.  Every spin wait is bounded: after
-// Q_WAIT_NS (or Q_SPIN_LIMIT polls) it records an error code in the device status word and
-// gives up, so a lost transaction never hangs the GPU.
+// g_qdev_wait_ns of wall time (2 s unless the host sets it, see
+// q_b200_set_wait_limit_ns) or Q_SPIN_LIMIT polls it records an error code in
+// the device status word and gives up, so a lost transaction never hangs the
+// GPU.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -13,9 +15,6 @@
 
 #ifndef Q_SPIN_LIMIT
 #define Q_SPIN_LIMIT (1u << 26)
-#endif
-#ifndef Q_WAIT_NS
-#define Q_WAIT_NS 2000000000ull  // 2 s
 #endif
 
 // Device status word (one per library load); 0 = OK.  Kernels write a code
@@ -35,6 +34,13 @@ enum : uint32_t {
 __device__ uint32_t g_qdev_status = 0;
 
 __device__ __forceinline__ void qdev_fail(uint32_t code) { atomicCAS(&g_qdev_status, 0u, code); }
+
+// Wall-time limit of every bounded wait, in ns (one per device; the host
+// may lower it, e.g. so a test can make a wait run out quickly).
+__device__ unsigned long long g_qdev_wait_ns = 2000000000ull;
+__device__ __forceinline__ unsigned long long qdev_wait_ns() {
+    return *reinterpret_cast<volatile unsigned long long*>(&g_qdev_wait_ns);
+}
 
 // Global nanosecond timer (bounds every wait in wall time).
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -96,17 +102,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait for phase `parity` of `bar`; false (and an error code) after
-// Q_WAIT_NS of wall time or Q_SPIN_LIMIT polls, whichever comes first.
+// g_qdev_wait_ns of wall time or Q_SPIN_LIMIT polls, whichever comes first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
     if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = gtimer();
+    const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
     for (uint32_t i = 0; i < Q_SPIN_LIMIT; ++i) {
-#ifdef Q_MBAR_NO_SLEEP  // experiment builds only
-        if (mbar_try_wait(bar, parity)) return true;
-#else
         if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
-#endif
-        if (gtimer() - t0 > Q_WAIT_NS) break;
+        if (gtimer() - t0 > lim) break;
     }
     qdev_fail(code);
     return false;

@@ -36,7 +36,7 @@
 // (per-slab ticket in global scratch), which adds the parts in CTA order.
 // Input prologue: coalesced loads staged in shared memory, then one thread
 // per 32-value block builds its limb fragment (rows padded to 144 bytes).
-// gemv_q4_kernel<true> adds the tensor-parallel exchange (GemvTp).
+// q4_slab_kernel<true> adds the tensor-parallel exchange (GemvTp).
 // Inside a CTA a producer warp streams stages through a shared-memory ring
 // with cp.async.bulk + mbarrier; weight loads start before the programmatic
 // dependent launch wait.  Consumer warp w handles the blocks of a slab with
@@ -61,11 +61,7 @@ struct StepParams {  // device-resident per-step scalars (graph-replay friendly)
     uint32_t valid;  // positions 0..valid-1 are unmasked for this row
 };
 
-#ifndef QB200_GEMV_CONSUMER_WARPS
-#define QB200_GEMV_CONSUMER_WARPS 15
-#endif
-static constexpr int GEMV_CONSUMER_WARPS = QB200_GEMV_CONSUMER_WARPS;
-#define QB200_GEMV_PER_SM_BOUND (QB200_GEMV_CONSUMER_WARPS <= 8 ? 2 : 1)
+static constexpr int GEMV_CONSUMER_WARPS = 15;
 static constexpr int GEMV_THREADS = GEMV_CONSUMER_WARPS * 32 + 32;
 static constexpr uint32_t GEMV_SLAB_ROWS = 32;     // rows per slab (two mma row groups)
 static constexpr uint32_t GEMV_BLOCK_BYTES = 640;  // one (slab, block) unit
@@ -104,18 +100,21 @@ struct GemvArgs {
 
 // Tensor-parallel exchange fused into the GEMVs (peer memory).  Each
 // rank's exchange area (at byte tp_off of every rank's buffer) holds
-// recv[2][W][tp_slice] fp32 | flag[2][W][GEMV_TP_MAX_CTAS] | ticket[2] u32.
+// recv[2][W][tp_slice] fp32 | flag[2][W][GEMV_TP_MAX_CTAS] | ticket[2] |
+// seq[2] u32 (seq[p]: receives of parity p this rank has completed).
 //   tp_send: the epilogue stores the finished rows (plus the residual on
 //   the rank whose epilogue adds it) into recv[tp_par][rank][row] of every
 //   rank instead of y, and CTA c, once its rows are stored, sets
-//   flag[tp_par][rank][c] = 1 on every rank (release, system scope; one
-//   word per CTA, so no two CTAs write the same remote word);
-//   tp_recv: every CTA's prologue waits (bounded) for the tp_expect flags
-//   of parity tp_par (W ranks x the sending grid); the last CTA past the
-//   wait (local ticket) clears them; each CTA then takes the input as the sum of the W slots in rank order (the
-//   bits a one-shot all-reduce would give).  A flag is set again only for
-//   the next exchange of the same parity, which needs this rank's next
-//   send, which runs after this grid.
+//   flag[tp_par][rank][c] = seq[tp_par] + 1 on every rank (release, system
+//   scope; one word per CTA, so no two CTAs write the same remote word);
+//   tp_recv: every CTA's prologue waits (bounded) until the tp_expect flags
+//   of parity tp_par (W ranks x the sending grid) reach seq[tp_par] + 1;
+//   the last CTA past the wait (local ticket) advances seq[tp_par]; each
+//   CTA then takes the input as the sum of the W slots in rank order (the
+//   bits a one-shot all-reduce would give).  Every rank runs the same
+//   exchanges, so the counts agree.  A slot is written again only by the
+//   next exchange of the same parity, whose send follows (in every rank's
+//   stream order) the receive of the exchange in between.
 struct GemvTp {
     uint8_t* tp_base[8];       // every rank's exchange buffer, mapped here
     uint32_t tp_off, tp_slice, tp_world, tp_rank;
@@ -137,7 +136,7 @@ struct GemvChain {
     uint32_t max_nb;            // largest nb of the phases (input-fragment table size)
     uint32_t* bar;              // n_phases counters, zero between launches (n_phases > 1)
     unsigned long long* trace;  // step-trace slot (null: off)
-    GemvTp tp;                  // single-phase launches of gemv_q4_kernel<true> only
+    GemvTp tp;                  // single-phase launches of q4_slab_kernel<true> only
 };
 
 // Shared memory: ring | bfrag[max_nb][144] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
@@ -228,30 +227,6 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const GemvTp& t
     }
 }
 
-#ifdef QB200_CHAIN_TS  // experiment builds only: per-CTA phase timestamps
-__device__ unsigned long long g_chain_ts[4 * 256 * 20];
-// one record per matrix shape class (QKV, wo, gate/up, other), so the last
-// launch of each class in a decode step stays readable
-__device__ __forceinline__ uint32_t chain_ts_kind(const GemvChain& c) {
-    const uint32_t M = c.ph[0].M, K = c.ph[0].K;
-    return M == 28672 ? 2u : (K == 4096 && M == 4096) ? 1u : (K == 4096 ? 0u : 3u);
-}
-__device__ __forceinline__ unsigned long long gtimer_fenced() {
-    unsigned long long t;
-#ifdef QB200_CHAIN_TS_CLOCK  // SM cycle counter: exact within a CTA, not comparable across CTAs
-    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t)::"memory");
-#else
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
-#endif
-    return t;
-}
-__shared__ uint32_t s_ts_base;  // record offset of this CTA, set at kernel entry
-#define CHAIN_TS(i) \
-    if (threadIdx.x == 0) g_chain_ts[s_ts_base + (i)] = gtimer_fenced()
-#else
-#define CHAIN_TS(i) ((void)0)
-#endif
-
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -296,7 +271,6 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
                                            uint32_t& ph, uint32_t pidx, bool dry,
                                            const PhaseRange& r) {
     constexpr uint32_t T = NW * 32;
-    if (!dry && pidx == 0) CHAIN_TS(6);
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t cta = blockIdx.x;
     const uint32_t nb = a.nb;
@@ -307,9 +281,6 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     const uint32_t own_lo[2] = {r.own_lo[0], r.own_lo[1]}, own_hi[2] = {r.own_hi[0], r.own_hi[1]};
 
     // ---- input prologue ------------------------------------------------------------
-    const uint32_t tsb = 4 * pidx;
-    (void)tsb;
-    if (!dry) CHAIN_TS(tsb + 0);
     const float* xs = a.x;
     if (a.gather) xs = a.x + (size_t)(dry ? 0u : a.step->token) * a.K;
     // Two steps.  (1) Coalesced: thread tid loads float4 number tid + T*r
@@ -331,30 +302,37 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         uint32_t* flag = reinterpret_cast<uint32_t*>(mine + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4) +
                          (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS;
         rx4 = reinterpret_cast<const float4*>(mine + (size_t)tpa.tp_par * tpa.tp_world * tpa.tp_slice * 4);
-        // flags of sending CTAs 0..tp_expect/W-1 of every rank; every CTA
-        // of this grid waits for all of them, the last one past the wait
-        // (local ticket) clears them
-        uint32_t* ticket = flag - (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS +
-                           (size_t)2 * tpa.tp_world * GEMV_TP_MAX_CTAS + tpa.tp_par;
+        // flags of sending CTAs 0..tp_expect/W-1 of every rank.  Flags carry
+        // the exchange's sequence number (this rank's count of completed
+        // receives of this parity, plus one): every CTA of this grid waits
+        // until each flag has reached it, then the last CTA past the wait
+        // (local ticket) advances the count.  Nothing is cleared, so a flag
+        // that lands late (after a timed-out wait) is below the next
+        // exchange's number and cannot release it.
+        uint32_t* ctl = flag - (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS +
+                        (size_t)2 * tpa.tp_world * GEMV_TP_MAX_CTAS;  // ticket[2] | seq[2]
+        uint32_t* ticket = ctl + tpa.tp_par;
+        uint32_t* seqw = ctl + 2 + tpa.tp_par;
+        const uint32_t want = __ldcg(seqw) + 1u;
         const uint32_t per = tpa.tp_expect / tpa.tp_world;
-        const unsigned long long t0 = gtimer();
+        const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
         for (uint32_t i = tid; i < tpa.tp_expect; i += T) {
             const uint32_t* f = flag + (size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per;
-            while (ld_acquire_sys(f) == 0u) {
-                if (gtimer() - t0 > Q_WAIT_NS) {
+            while ((int32_t)(ld_acquire_sys(f) - want) < 0) {
+                if (gtimer() - t0 > lim) {
                     qdev_fail(QDEV_PEER_TIMEOUT);
                     break;
                 }
             }
         }
-        __shared__ uint32_t s_tp_last;
         asm volatile("bar.sync 1, %0;" ::"r"(T));
-        if (tid == 0) s_tp_last = atomicAdd(ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
-        asm volatile("bar.sync 1, %0;" ::"r"(T));
-        if (s_tp_last) {
-            // no rank sets these again before this grid has finished
-            for (uint32_t i = tid; i < tpa.tp_expect; i += T) flag[(size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per] = 0u;
-            if (tid == 0) *ticket = 0u;
+        if (tid == 0) {
+            uint32_t old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
+            if (old == gridDim.x - 1) {  // every CTA has read `want`
+                *ticket = 0u;
+                __stcg(seqw, want);
+            }
         }
     }
     for (uint32_t base = 0; base < n4; base += T * NR) {
@@ -388,17 +366,6 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
                 }
             }
         }
-#ifdef QB200_CHAIN_TS
-        if (tid == 0 && base == 0 && pidx == 0 && !dry) {
-            unsigned long long t;
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tsetp.eq.f32 p, %1, 0f7F7FFFFF;\n\t"
-                "@p st.volatile.global.u32 [%2], 0;\n\t}"
-                ::"l"(0ull), "f"(xv[0].x), "l"(g_chain_ts + 5119) : "memory");
-            t = gtimer_fenced();
-            g_chain_ts[s_ts_base + 8] = t;
-        }
-#endif
         if (a.x_copy && cta == 0 && !dry) {
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
@@ -452,7 +419,6 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
-    if (!dry && pidx == 0) CHAIN_TS(9);
     for (uint32_t b = tid; b < nbk; b += T) {
         float v[32];
         const uint8_t* src = bfrag + (size_t)b * GEMV_BFRAG_BYTES;
@@ -528,7 +494,6 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
     if (dry) return;
-    CHAIN_TS(tsb + 1);
 
     // ---- main loop ---------------------------------------------------------------
     const uint32_t g = lane >> 2, t = lane & 3;
@@ -605,20 +570,14 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     float2 acc = make_float2(0.0f, 0.0f), acc2 = make_float2(0.0f, 0.0f);  // rows g, g+8 | g+16, g+24
     // running ring slot / parity and current slab (no divisions per stage)
     uint32_t j = j_first, jb = j_first * nb;
-    if (pidx == 0) CHAIN_TS(10);
     for (uint32_t sb0 = x0; sb0 < x1; sb0 += c.stage_blocks) {
-        if (sb0 == x0 && pidx == 0) CHAIN_TS(11);
         mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT);
-        if (sb0 == x0 && pidx == 0) CHAIN_TS(15);
         const uint32_t sb1 = min(sb0 + c.stage_blocks, x1);
         for (uint32_t seg = sb0; seg < sb1;) {
             const uint32_t seg_end = min(sb1, jb + nb);
             // this warp's blocks of the segment: (b - jb) % NW == warp
             const uint32_t b = seg + ((warp + NW - (seg - jb) % NW) % NW);
             int n = b < seg_end ? (int)((seg_end - b + NW - 1) / NW) : 0;
-#ifdef QB200_GEMV_NO_COMPUTE  // experiment builds only: stream without arithmetic
-            n = 0;
-#endif
             uint32_t qo = ring_off + s * stage_bytes + (b - sb0) * GEMV_BLOCK_BYTES + lane * 16;
             uint32_t bo = bfrag_off + (b - jb) * GEMV_BFRAG_BYTES;
             uint32_t fo = fsc_off + (b - jb) * GEMV_FSC_BYTES;
@@ -677,24 +636,27 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
             ph ^= 1;
         }
     }
-    CHAIN_TS(tsb + 2);
     if (jl) reduce_batch(jl);
     asm volatile("bar.sync 1, %0;" ::"r"(T));  // tables and red[] free for the next phase
     if (TP && tpa.tp_send && tid < tpa.tp_world) {
         // every row this CTA finished is stored (bar.sync above): publish to
         // rank tid
+        // (flag value: this exchange's sequence number, from this rank's
+        // own receive count of the parity; every rank counts the same)
+        const uint32_t* own = reinterpret_cast<const uint32_t*>(
+            tpa.tp_base[tpa.tp_rank] + tpa.tp_off + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4);
+        const uint32_t seq = __ldcg(own + (size_t)2 * tpa.tp_world * GEMV_TP_MAX_CTAS + 2 + tpa.tp_par) + 1u;
         __threadfence_system();
         uint32_t* f = reinterpret_cast<uint32_t*>(tpa.tp_base[tid] + tpa.tp_off + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4);
-        st_release_sys(f + ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * GEMV_TP_MAX_CTAS + cta, 1u);
+        st_release_sys(f + ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * GEMV_TP_MAX_CTAS + cta, seq);
     }
-    CHAIN_TS(tsb + 3);
 }
 
 // TP: the single-phase tensor-parallel form (c.tp: exchange fused into
 // the epilogue / prologue); the other instantiation carries none of it.
 template <bool TP>
-__global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
-    gemv_q4_kernel(const __grid_constant__ GemvChain c) {
+__global__ void __launch_bounds__(GEMV_THREADS, 1)
+    q4_slab_kernel(const __grid_constant__ GemvChain c) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t NW = GEMV_CONSUMER_WARPS, T = NW * 32;
     const uint32_t stage_bytes = c.stage_blocks * GEMV_BLOCK_BYTES;
@@ -728,12 +690,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
     }
     __shared__ PhaseRange s_rng[GEMV_MAX_PHASES];
     if (tid < P) s_rng[tid] = phase_range(c.ph[tid].n_slabs, c.ph[tid].nb, cta, G);
-#ifdef QB200_CHAIN_TS
-    if (tid == 0) s_ts_base = chain_ts_kind(c) * 5120 + blockIdx.x * 20;
-#endif
     __syncthreads();
     if (tid == 0) trace_mark(c.trace, 0);
-    CHAIN_TS(12);
     pdl_trigger();
 
     if (tid >= T) {
@@ -743,10 +701,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
             uint32_t s = 0, ph = 0, k = 0;  // ring slot, its parity, stages issued
             bool ok = true;
             for (uint32_t p = 0; p < P && ok; ++p) {
-#ifdef QB200_CHAIN_NOPREFETCH  // experiment builds only: no weight prefetch across barriers
-                if (p > 0)
-                    while (ld_acquire_u32(c.bar + p - 1) < G) __nanosleep(32);
-#endif
                 const GemvArgs& a = s_args[p];
                 const uint32_t x0 = s_rng[p].x0, x1 = s_rng[p].x1;
                 for (uint32_t b0 = x0; b0 < x1; b0 += c.stage_blocks, ++k) {
@@ -755,28 +709,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
                         break;
                     }
                     const uint32_t n = min(c.stage_blocks, x1 - b0);
-#ifdef QB200_GEMV_NO_LOAD  // experiment builds only: consumers run on stale shared memory
-                    (void)pol;
-                    mbar_arrive(&full[s]);
-#else
                     mbar_arrive_expect_tx(&full[s], n * GEMV_BLOCK_BYTES);
                     bulk_g2s(ring + (size_t)s * stage_bytes, a.w + (size_t)b0 * GEMV_BLOCK_BYTES,
                              n * GEMV_BLOCK_BYTES, &full[s], pol);
-#endif
                     if (++s == c.n_stage) {
                         s = 0;
                         ph ^= 1;
                     }
                 }
             }
-#ifdef QB200_CHAIN_TS
-            g_chain_ts[s_ts_base + 14] = gtimer_fenced();
-#endif
         }
-#ifdef QB200_CHAIN_TS
-        if (tid == T + 1 && mbar_wait(&full[0], 0, QDEV_WAIT_FULL_TIMEOUT))
-            g_chain_ts[s_ts_base + 13] = gtimer_fenced();
-#endif
         pdl_wait();  // every thread waits: the grid ends after its predecessor
         return;
     }
@@ -794,29 +736,23 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
         if (it == 1) {
             pdl_wait();
             if (tid == 0) trace_mark(c.trace, 1);
-            CHAIN_TS(16);
-            CHAIN_TS(7);
         }
         if (p > 0) {
             // grid barrier: every CTA has finished phase p - 1 (outputs written)
             if (tid == 0) {
-                const unsigned long long t0 = gtimer();
+                const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
                 while (ld_acquire_u32(c.bar + p - 1) < G) {
-                    if (gtimer() - t0 > Q_WAIT_NS) {
+                    if (gtimer() - t0 > lim) {
                         qdev_fail(QDEV_GRID_TIMEOUT);
                         break;
                     }
-#ifndef QB200_CHAIN_SPIN  // experiment builds only: poll without sleeping
                     __nanosleep(32);
-#endif
                 }
             }
-            if (p == 2) CHAIN_TS(19);
             asm volatile("bar.sync 1, %0;" ::"r"(T));
         }
         gemv_phase<NW, TP>(s_args[p], c, smem, bfrag, fsc, red, full, empty, rms_part, s, ph, p, dry, s_rng[p]);
         if (dry) continue;
-        if (p == 1) CHAIN_TS(18);
         if (p + 1 < P && tid == 0) {
             // consumers passed bar.sync at the end of the phase, so this
             // release covers every consumer thread's outputs
@@ -833,7 +769,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, QB200_GEMV_PER_SM_BOUND)
         }
     }
     if (tid == 0) trace_mark(c.trace, 2);
-    CHAIN_TS(17);
 }
 
 // Repack upstream AoS Q4_0 blocks ([M][nb] x 20 B) into slab tiles.

@@ -70,6 +70,7 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
         if (r != Q_OK) return r;
         if (!cuda_ok(cudaMemset(sp, 0, sb), "memset(gemv scratch)")) return Q_ERR_INVALID_ARG;
         s->gemv_scratch = sp;
+        register_zero_area(sp, ChainPlan::kTicketWords * 4);
     }
     cudaStream_t st = s->stream;
     const size_t nbD = D / 32, nbH = H / 32;
@@ -215,6 +216,7 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
         return Q_ERR_ARENA_OOM;
     }
     s->arena_base = s->arena_head;
+    register_zero_area(s->chain_bar, (size_t)L * GEMV_MAX_PHASES * 4);
     if (!cuda_ok(cudaMemsetAsync(s->best, 0, 8, st), "init") ||
         !cuda_ok(cudaMemsetAsync(s->chain_bar, 0, (size_t)L * GEMV_MAX_PHASES * 4, st), "init") ||
         !cuda_ok(cudaMemsetAsync(s->tok_count, 0, 4, st), "init") ||
@@ -272,10 +274,7 @@ q_error_code plan_attention(DevState* s) {
     const void* kern = attn_kernel_for(s->hd, G);
     if (!kern || G == 0 || G > (uint32_t)ATT_MAXG) return Q_ERR_INVALID_CONFIG;
     const size_t limit = 227 * 1024 - 8 * 1024;  // dynamic shared memory beside the static part
-#ifndef QB200_ATTN_MAX_CS
-#define QB200_ATTN_MAX_CS 16
-#endif
-    for (uint32_t cs = QB200_ATTN_MAX_CS; cs >= 2; cs /= 2) {
+    for (uint32_t cs = 16; cs >= 2; cs /= 2) {
         if (cs > 8 &&
             cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
             cudaGetLastError();
@@ -307,10 +306,6 @@ q_error_code plan_attention(DevState* s) {
                 continue;
             }
             if (n < (int)s->tp.nkv && !(cs == 2 && slots == 2 && n >= 1)) continue;
-#ifdef QB200_ATTN_PHASES
-            fprintf(stderr, "plan_attention: cluster %u slots %u chunk_alloc %u smem %zu active clusters %d\n",
-                    cs, slots, ca, smem, n);
-#endif
             s->att_cs = cs;
             s->att_ca = ca;
             s->att_slots = slots;
@@ -433,9 +428,6 @@ static cudaError_t nccl_status(ncclResult_t r) {
 // In-place sum of `count` floats over the tensor-parallel ranks (no-op alone).
 static cudaError_t allreduce_sum(DevState* s, float* buf, size_t count, cudaStream_t st) {
     if (s->tp_world == 1) return cudaSuccess;
-#ifdef QB200_TP_NO_ALLREDUCE  // experiment builds only: timing without the collective (wrong results)
-    return cudaSuccess;
-#endif
     if (s->peers_ready) return tp_allreduce(s, buf, (uint32_t)count, TP_SUM_F32, st);
     const NcclApi* n = nccl();
     if (!n) return cudaErrorUnknown;

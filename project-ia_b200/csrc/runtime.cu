@@ -3,6 +3,7 @@
 #include <cmath>
 #include <cstdio>
 #include <set>
+#include <tuple>
 
 #include "runtime.cuh"
 
@@ -66,16 +67,51 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
     return e;
 }
 
-q_error_code check_device_status(const char* where) {
+// ---- areas kernels leave zero between launches --------------------------------
+
+static std::mutex g_zero_mu;
+static std::vector<std::tuple<int, void*, size_t>> g_zero_areas;  // (device, ptr, bytes)
+
+void register_zero_area(void* p, size_t bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_zero_mu);
+    g_zero_areas.emplace_back(dev, p, bytes);
+}
+
+void unregister_zero_area(void* p) {
+    std::lock_guard<std::mutex> lk(g_zero_mu);
+    g_zero_areas.erase(std::remove_if(g_zero_areas.begin(), g_zero_areas.end(),
+                                      [p](const auto& t) { return std::get<1>(t) == p; }),
+                       g_zero_areas.end());
+}
+
+uint32_t take_device_status() {
     uint32_t st = 0;
-    if (!cuda_ok(cudaMemcpyFromSymbol(&st, g_qdev_status, sizeof st), where)) return Q_ERR_INVALID_ARG;
+    if (cudaMemcpyFromSymbol(&st, g_qdev_status, sizeof st) != cudaSuccess) return QDEV_BAD_ARG;
+    if (st == 0) return 0;
+    // A wait that gave up may have left tickets or barrier counters
+    // non-zero; the next launch needs them zero.  Everything in flight on
+    // the device finishes first.
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceSynchronize();
+    {
+        std::lock_guard<std::mutex> lk(g_zero_mu);
+        for (const auto& t : g_zero_areas)
+            if (std::get<0>(t) == dev) cudaMemset(std::get<1>(t), 0, std::get<2>(t));
+    }
+    const uint32_t zero = 0;
+    cudaMemcpyToSymbol(g_qdev_status, &zero, sizeof zero);
+    cudaDeviceSynchronize();
+    return st;
+}
+
+q_error_code check_device_status(const char* where) {
+    const uint32_t st = take_device_status();
     if (st != 0) {
-        {
-            std::lock_guard<std::mutex> lk(g_err_mu);
-            g_last_error = std::string(where) + ": device wait timed out (code " + std::to_string(st) + ")";
-        }
-        uint32_t zero = 0;
-        cudaMemcpyToSymbol(g_qdev_status, &zero, sizeof zero);
+        std::lock_guard<std::mutex> lk(g_err_mu);
+        g_last_error = std::string(where) + ": device wait timed out (code " + std::to_string(st) + ")";
         return Q_ERR_INVALID_ARG;
     }
     return Q_OK;
@@ -102,22 +138,15 @@ bool plan_gemv(uint32_t M, uint32_t K, GemvPlan& p) {
 // as fit.
 bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
     if (n == 0 || n > (uint32_t)GEMV_MAX_PHASES) return false;
-#ifndef QB200_GEMV_PER_SM
-#define QB200_GEMV_PER_SM 1
-#endif
-#ifndef QB200_GEMV_MAX_STAGES
-#define QB200_GEMV_MAX_STAGES 8
-#endif
-    uint64_t grid = (uint64_t)QB200_GEMV_PER_SM * device_sms();
+    constexpr uint32_t kMaxStages = 8;      // ring depth cap
+    constexpr uint32_t kWholeSlabPct = 60;  // smallest whole-slab grid, % of the SMs
+    uint64_t grid = device_sms();  // one CTA per SM
     uint32_t max_nb = 0;
     for (uint32_t i = 0; i < n; ++i) {
         grid = std::min<uint64_t>(grid, mats[i]->NB());
         max_nb = std::max(max_nb, mats[i]->nb);
     }
     if (grid == 0) return false;
-#ifndef QB200_WHOLE_SLAB_PCT
-#define QB200_WHOLE_SLAB_PCT 60
-#endif
     // Whole slabs: a grid that divides the slab count gives every CTA the
     // same whole slabs, so no slab is split across CTAs and no partial sums
     // or tickets are needed.  Worth it while the grid still covers most
@@ -127,7 +156,7 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
         const uint64_t ns = mats[0]->n_slabs;
         for (uint64_t d = std::min<uint64_t>(grid, ns); d >= 1; --d) {
             if (ns % d) continue;
-            if (d * 100 >= (uint64_t)device_sms() * QB200_WHOLE_SLAB_PCT) grid = d;
+            if (d * 100 >= (uint64_t)device_sms() * kWholeSlabPct) grid = d;
             break;
         }
     }
@@ -149,16 +178,12 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
         red_slabs = std::max<uint32_t>(red_slabs, (uint32_t)std::min<uint64_t>(8, (range + m.nb - 1) / m.nb + 1));
     }
     cp.red_slabs = red_slabs;
-    const size_t budget = QB200_GEMV_PER_SM == 1 ? 220 * 1024 : 113 * 1024;
+    const size_t budget = 220 * 1024;
     const size_t fixed = gemv_smem_bytes(max_nb, 0, 0, red_slabs);
     if (fixed >= budget) return false;
-#ifdef QB200_GEMV_STAGE_BLOCKS
-    const uint32_t sizes[] = {QB200_GEMV_STAGE_BLOCKS};
-#else
     const uint32_t sizes[] = {256, 192, 128, 64};
-#endif
     for (uint32_t sb : sizes) {
-        const uint32_t ns = (uint32_t)std::min<size_t>(QB200_GEMV_MAX_STAGES,
+        const uint32_t ns = (uint32_t)std::min<size_t>(kMaxStages,
                                                        (budget - fixed) / ((size_t)sb * GEMV_BLOCK_BYTES));
         if (ns >= 2) {
             cp.stage_blocks = sb;
@@ -197,7 +222,7 @@ cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const
     const bool fused = tp && (tp->tp_send || tp->tp_recv);
     if (fused && cp.n != 1) return cudaErrorInvalidValue;
     if (fused) c.tp = *tp;
-    const void* kern = fused ? (const void*)gemv_q4_kernel<true> : (const void*)gemv_q4_kernel<false>;
+    const void* kern = fused ? (const void*)q4_slab_kernel<true> : (const void*)q4_slab_kernel<false>;
     cudaError_t e = ensure_smem_attr(kern, 227 * 1024);
     if (e != cudaSuccess) return e;
     // Phases after the first wait on the whole grid: all CTAs must be
@@ -257,6 +282,7 @@ void* op_gemv_scratch(size_t bytes) {
     if (b.second < bytes) {
         if (b.first) {
             cudaDeviceSynchronize();
+            unregister_zero_area(b.first);
             cudaFree(b.first);
         }
         b = {nullptr, 0};
@@ -264,6 +290,7 @@ void* op_gemv_scratch(size_t bytes) {
         if (!cuda_ok(cudaMalloc(&q, bytes), "cudaMalloc(gemv scratch)")) return nullptr;
         if (!cuda_ok(cudaMemset(q, 0, bytes), "memset(gemv scratch)")) return nullptr;
         b = {q, bytes};
+        register_zero_area(q, ChainPlan::kTicketWords * 4);
     }
     return b.first;
 }
@@ -325,6 +352,10 @@ void free_model(DevState* s) {
     s->trace_buf = nullptr;
     s->g_body = s->g_full = s->g_trace = nullptr;
     s->graph_kv = nullptr;
+    if (s->gemv_scratch) unregister_zero_area(s->gemv_scratch);
+    if (s->chain_bar) unregister_zero_area(s->chain_bar);
+    s->gemv_scratch = nullptr;
+    s->chain_bar = nullptr;
     for (void* p : s->weight_allocs) cudaFree(p);
     s->weight_allocs.clear();
     s->qkv.clear();

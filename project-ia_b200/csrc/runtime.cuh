@@ -161,6 +161,14 @@ q_error_code ensure_graphs(q_context* ctx, DevState* s);
 q_error_code plan_attention(DevState* s);
 q_error_code capture_trace_graph(q_context* ctx, DevState* s);
 q_error_code check_device_status(const char* where);
+// Reads and clears the device status word of the current device (0 = no
+// wait ran out); when it was set, re-zeroes every registered ticket area of
+// the device first.
+uint32_t take_device_status();
+// Ticket / barrier-counter areas that kernels leave zero between launches
+// (re-zeroed by take_device_status after a wait ran out).
+void register_zero_area(void* p, size_t bytes);
+void unregister_zero_area(void* p);
 cudaError_t tp_allreduce(DevState* s, void* data, uint32_t n, int op, cudaStream_t st,
                          float* out = nullptr);
 void free_model(DevState* s);

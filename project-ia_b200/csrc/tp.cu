@@ -86,9 +86,9 @@ __global__ void __launch_bounds__(512) tp_allreduce_kernel(const TpArgs a) {
     }
     // 2. every rank's slice has arrived here
     if (tid < W) {
-        const unsigned long long t0 = gtimer();
+        const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
         while (ld_acquire_sys(myflags + par * W + tid) < q) {
-            if (gtimer() - t0 > Q_WAIT_NS) {
+            if (gtimer() - t0 > lim) {
                 qdev_fail(QDEV_PEER_TIMEOUT);
                 break;
             }

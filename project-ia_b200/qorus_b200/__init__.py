@@ -141,6 +141,9 @@ _SIGS = {
     "q_b200_tp_ipc_handle": (_i, [_vp, _vp, _sz]),
     "q_b200_tp_ipc_open": (_i, [_vp, _vp, _sz]),
     "q_b200_tp_shape": (_i, [_vp, _u32, _u32, _vp, _u32]),
+    "q_b200_set_wait_limit_ns": (_i, [_u64]),
+    "q_b200_device_status": (_u32, []),
+    "q_b200_selftest_exchange_timeout": (_i, [_u64, _vp]),
     "q_b200_kernel_launches": (_u64, []),
     "q_b200_last_error": (C.c_char_p, []),
 }

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes as C
 import hashlib
+import os
 import shutil
 import sys
 import tempfile
@@ -32,7 +33,8 @@ sys.path.insert(0, str(ROOT / "oracle"))
 import oracle as O  # noqa: E402
 import qorus_b200 as Q  # noqa: E402
 
-UPSTREAM = Path("/root/reference")
+# the upstream source tree: $QORUS_REFERENCE, else a "reference" directory beside this repository
+UPSTREAM = Path(os.environ.get("QORUS_REFERENCE", str(Path(__file__).resolve().parents[3] / "reference")))
 OUT = Path(__file__).resolve().parent
 
 

@@ -3,6 +3,7 @@ headers declare, its structs have upstream's layout, the host-side logic
 (file parsing, validation order, generators, greedy sampling) behaves like
 upstream.  No call here launches a kernel."""
 import ctypes as C
+import os
 import re
 import subprocess
 from pathlib import Path
@@ -13,7 +14,8 @@ import qorus_b200 as Q
 from conftest import ROOT
 
 HEADERS = [ROOT / "include" / "qorus.h", ROOT / "include" / "qorus_b200.h"]
-UPSTREAM_INCLUDE = Path("/root/reference/include")
+# upstream headers: $QORUS_REFERENCE/include, else a "reference" directory beside this repository
+UPSTREAM_INCLUDE = Path(os.environ.get("QORUS_REFERENCE", str(Path(__file__).resolve().parents[2] / "reference"))) / "include"
 
 
 def declared_functions():

@@ -168,3 +168,42 @@ def test_profile_step_stamps_and_result(tiny_path, golden):
     dev.kv_read(kv_plain)
     assert np.array_equal(kv_traced, kv_plain)
     dev.close()
+
+
+def test_llama8b_full_decode_32_steps_vs_oracle(tmp_path):
+    """The benchmarked configuration itself: 32 layers,
+    dim 4096, 32/8 heads, FFN 14336, vocab 128256, KV cache pre-filled with
+    2048 positions of N(0,1), then 32 greedy steps through llama_forward,
+    each step's logits against the oracle's (max-abs <= 1e-2, same argmax),
+    and the 32 new KV rows of every layer within the per-kernel bar."""
+    import os
+    from pathlib import Path
+    shm = Path("/dev/shm")
+    d = shm if shm.exists() and os.access(shm, os.W_OK) else tmp_path
+    npos, steps = 2048, 32
+    cfg = Q.config(128256, 4096, 14336, 32, 32, 8, npos + 64)
+    path = d / f"qorus_parity_l8b_{os.getpid()}.qorus"
+    try:
+        Q.write_model(str(path), cfg, seed=0)
+        dev = Q.Model(str(path))
+        orc = O.OracleModel(str(path), threads=os.cpu_count() or 1)
+        assert Q.lib.q_b200_fill_kv_prefill(Q.ptr(orc.kv), C.byref(cfg), npos, 1, 0) == 0
+        dev.kv_write(orc.kv)
+        tok, worst = 1, 0.0
+        for step in range(steps):
+            a = dev.forward(np.array([tok], np.uint32), npos + step)
+            b = orc.forward(np.array([tok], np.uint32), npos + step)
+            worst = max(worst, float(np.abs(a - b).max()))
+            assert np.abs(a - b).max() <= LOGIT_TOL, f"step {step}: {np.abs(a - b).max():.3e}"
+            assert int(np.argmax(a)) == int(np.argmax(b)), f"step {step}"
+            tok = int(np.argmax(b))
+        kv = np.zeros(orc.kv.size, np.float32)
+        dev.kv_read(kv)
+        hd = 128
+        shp = (cfg.n_layers, cfg.n_kv_heads, cfg.max_seq_len, 2 * hd)
+        kv_close(kv.reshape(shp)[:, :, npos: npos + steps], orc.kv.reshape(shp)[:, :, npos: npos + steps])
+        dev.close()
+        orc.close()
+    finally:
+        if path.exists():
+            path.unlink()

@@ -1,6 +1,7 @@
 """Tensor parallelism on 2 GPUs (skipped on single-GPU machines): two ranks,
 one process per GPU, each holding its shard; the decode graph all-reduces
-either over NVLink peer memory (CUDA IPC) or with NCCL.  The gathered logits and greedy tokens must match the upstream
+either over NVLink peer memory (CUDA IPC; fused into the GEMVs, or the
+separate exchange kernel with QORUS_B200_TP_FUSED=0) or with NCCL.  The gathered logits and greedy tokens must match the upstream
 kernels' golden outputs for the tiny config (logits max-abs <= 1e-2,
 identical tokens), and each rank's KV cache (its own KV heads) must match
 the CPU oracle's rows for those heads."""
@@ -24,7 +25,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, path, prompt, ipc, out):
+def _worker(rank, world, port, path, prompt, ipc, fused, out):
+    os.environ["QORUS_B200_TP_FUSED"] = "1" if fused else "0"
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -54,8 +56,9 @@ def _worker(rank, world, port, path, prompt, ipc, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("ipc", [True, False], ids=["peer-memory", "nccl"])
-def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden, ipc):
+@pytest.mark.parametrize("ipc,fused", [(True, True), (True, False), (False, False)],
+                         ids=["peer-memory-fused", "peer-memory-kernel", "nccl"])
+def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden, ipc, fused):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -64,7 +67,7 @@ def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden, ipc):
     q = ctx.Queue()
     port = _free_port()
     prompt = golden["tiny_prompt"]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, tiny_path, prompt, ipc, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, tiny_path, prompt, ipc, fused, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
