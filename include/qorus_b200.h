@@ -143,6 +143,16 @@ q_error_code q_b200_gemv_q4(const void* d_packed, uint32_t M, uint32_t K,
 q_error_code q_b200_gemv_q4_noalloc(const void* d_packed, uint32_t M, uint32_t K,
                                     const float* d_x, float* d_y, void* stream);
 
+/* The same Q4_0 product over n_rows input rows at once: d_y[r][m] =
+ * sum_k W[m][k] d_x[r][k] for r < n_rows (d_x [n_rows][K], d_y [n_rows][M],
+ * fp32, 16-byte aligned).  This is the prompt-path contraction: upstream
+ * runs q_gemv_q4_f32_avx2 (src/ops/avx2/matmul.c:98-271) once per prompt
+ * row (src/models/model.c:1120-1165); here the rows go through one
+ * tensor-core GEMM (tcgen05) with fp16 hi/lo operand halves (an fp32-grade
+ * result).  Allocates a workspace on first use (grown, then kept). */
+q_error_code q_b200_gemm_q4(const void* d_packed, uint32_t M, uint32_t K, const float* d_x,
+                            uint32_t n_rows, float* d_y, void* stream);
+
 /* FP32 GEMV y[M] = W[M,K] x[K] (the LM head of upstream
  * src/models/model.c:1821-1844, dot order of src/ops/avx2/matmul_fp32.c). */
 q_error_code q_b200_gemv_f32(const float* d_w, uint32_t M, uint32_t K,

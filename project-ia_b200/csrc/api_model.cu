@@ -168,6 +168,15 @@ static q_error_code ready(q_llama_model* model, q_context* ctx, DevState** out) 
     return Q_OK;
 }
 
+// Prompts of more than one row on a single-GPU context take the tensor-core
+// prefill path (csrc/prefill.cu); QORUS_B200_PREFILL=0 forces the row replay
+// below, as do tensor-parallel contexts.
+static bool use_prefill(const DevState* s, uint32_t seq_len) {
+    if (seq_len < 2 || s->tp_world != 1) return false;
+    const char* e = std::getenv("QORUS_B200_PREFILL");
+    return !(e && e[0] == '0');
+}
+
 // One graph replay per row: rows 0..seq_len-2 run the layer stack only, the
 // last row also runs the LM head + argmax.  Row t sees the upstream softmax
 // row length N = pos + seq_len and unmasked positions 0..pos+t.
@@ -203,7 +212,11 @@ q_error_code llama_forward(q_llama_model* model, q_context* ctx, const uint32_t*
     q_error_code rc = ready(model, ctx, &s);
     if (rc != Q_OK) return rc;
     Q_CUDA(cudaStreamSynchronize(s->stream));  // pinned step slots may still be in use
-    if ((rc = run_rows(s, tokens, seq_len, pos)) != Q_OK) return rc;
+    if (use_prefill(s, seq_len))
+        rc = run_prefill(s, (float*)ctx->kv_buffer, tokens, seq_len, pos);
+    else
+        rc = run_rows(s, tokens, seq_len, pos);
+    if (rc != Q_OK) return rc;
     if ((rc = gather_logits(s)) != Q_OK) return rc;
     Q_CUDA(cudaMemcpyAsync(logits, s->tp_world > 1 ? s->logits_all : s->logits,
                            (size_t)model->config.vocab_size * 4, cudaMemcpyDeviceToHost, s->stream));
@@ -253,7 +266,11 @@ q_error_code q_generate(q_generation_state* st) {
     q_error_code rc = ready(st->model, st->ctx, &s);
     if (rc != Q_OK) return rc;
     Q_CUDA(cudaStreamSynchronize(s->stream));
-    if ((rc = run_rows(s, st->prompt_tokens, st->num_prompt_tokens, 0)) != Q_OK) return rc;
+    if (use_prefill(s, st->num_prompt_tokens))
+        rc = run_prefill(s, (float*)st->ctx->kv_buffer, st->prompt_tokens, st->num_prompt_tokens, 0);
+    else
+        rc = run_rows(s, st->prompt_tokens, st->num_prompt_tokens, 0);
+    if (rc != Q_OK) return rc;
     st->current_pos = st->num_prompt_tokens;
     while (st->num_generated_tokens < st->max_tokens) {
         if (st->current_pos >= c.max_seq_len) break;

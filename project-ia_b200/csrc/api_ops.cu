@@ -266,6 +266,65 @@ void q_dequantize_q4_0_block_avx2_public(const q_block_q4_0* block, float* outpu
 
 }  // extern "C"
 
+// ---- Q4_0 GEMM over many rows (the prefill contraction) ------------------------------
+
+namespace {
+struct GemmWork {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+}  // namespace
+
+extern "C" q_error_code q_b200_gemm_q4(const void* d_packed, uint32_t M, uint32_t K, const float* d_x,
+                                       uint32_t n_rows, float* d_y, void* stream) {
+    if (!d_packed || !d_x || !d_y) return Q_ERR_INVALID_ARG;
+    if (n_rows == 0) return Q_ERR_INVALID_SIZE;
+    if ((const void*)d_x == (const void*)d_y) return Q_ERR_ALIASING;
+    if (((uintptr_t)d_x & 15) || ((uintptr_t)d_packed & 15) || ((uintptr_t)d_y & 15)) return Q_ERR_MISALIGNED;
+    GemvPlan p;
+    if (!plan_gemv(M, K, p)) return Q_ERR_INVALID_SIZE;
+    // workspace: activation halves [2][n][K], weight halves [2][M][K], scales
+    static std::mutex mu;
+    static std::unordered_map<int, GemmWork> work;
+    std::lock_guard<std::mutex> lk(mu);
+    int dev = 0;
+    Q_CUDA(cudaGetDevice(&dev));
+    const size_t b_act = ((size_t)2 * n_rows * K * 2 + 255) / 256 * 256;
+    const size_t b_w = ((size_t)2 * M * K * 2 + 255) / 256 * 256;
+    const size_t b_ts = ((size_t)n_rows * 4 + 255) / 256 * 256, b_rs = ((size_t)M * 4 + 255) / 256 * 256;
+    const size_t need = b_act + b_w + b_ts + b_rs;
+    GemmWork& w = work[dev];
+    cudaStream_t st = (cudaStream_t)stream;
+    if (w.bytes < need) {
+        Q_CUDA(cudaDeviceSynchronize());
+        if (w.p) cudaFree(w.p);
+        w = GemmWork{};
+        if (!cuda_ok(cudaMalloc(&w.p, need), "cudaMalloc(gemm workspace)")) return Q_ERR_ALLOC_FAILED;
+        w.bytes = need;
+    }
+    uint8_t* base = (uint8_t*)w.p;
+    DevState tmp;  // only the prefill workspace fields are used
+    tmp.pf_act = (__half*)base;
+    tmp.pf_w = (__half*)(base + b_act);
+    tmp.pf_tscale = (float*)(base + b_act + b_w);
+    tmp.pf_rscale = (float*)(base + b_act + b_w + b_ts);
+    ActSplitArgs as{};
+    as.x = d_x;
+    as.ldx = K;
+    as.K = K;
+    as.hi = tmp.pf_act;
+    as.lo = tmp.pf_act + (size_t)n_rows * K;
+    as.tscale = tmp.pf_tscale;
+    Q_CUDA(launch_act_split(&tmp, as, n_rows, st));
+    Q_CUDA(launch_w_split(&tmp, (const uint8_t*)d_packed, p, st));
+    PfGemmArgs g{};
+    g.epi = EPI_STORE;
+    g.y = d_y;
+    g.ldy = M;
+    Q_CUDA(launch_pf_gemm(&tmp, n_rows, M, K, g, st));
+    return Q_OK;
+}
+
 // ---- device status and bounded waits ---------------------------------------------
 
 extern "C" {

@@ -4,6 +4,7 @@
 #include "runtime.cu"
 #include "tp.cu"
 #include "model.cu"
+#include "prefill.cu"
 #include "api.cu"
 #include "api_model.cu"
 #include "api_ops.cu"

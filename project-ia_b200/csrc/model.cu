@@ -320,7 +320,7 @@ q_error_code plan_attention(DevState* s) {
 // 3-D tensor map over the whole KV cache: x = the 2*hd floats of a position
 // (K then V), y = position, z = layer * n_kv + kv head.  Boxes of
 // ATT_STAGE_BYTES: hd floats by ATT_STAGE_BYTES / (4 hd) positions.
-static q_error_code make_kv_map(DevState* s, void* kv) {
+PFN_cuTensorMapEncodeTiled tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled encode = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -330,10 +330,13 @@ static q_error_code make_kv_map(DevState* s, void* kv) {
             q == cudaDriverEntryPointSuccess)
             encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
     });
-    if (!encode) {
-        set_last_error("cuTensorMapEncodeTiled unavailable", cudaErrorNotSupported);
-        return Q_ERR_INVALID_ARG;
-    }
+    if (!encode) set_last_error("cuTensorMapEncodeTiled unavailable", cudaErrorNotSupported);
+    return encode;
+}
+
+static q_error_code make_kv_map(DevState* s, void* kv) {
+    const PFN_cuTensorMapEncodeTiled encode = tensor_map_encoder();
+    if (!encode) return Q_ERR_INVALID_ARG;
     const q_llama_config& c = s->cfg;
     const uint32_t hd = s->hd;
     // (a tensor-parallel rank's cache holds its own KV heads only)
@@ -518,10 +521,12 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
     return e;
 }
 
-static cudaError_t enqueue_head(DevState* s, cudaStream_t st) {
+// LM head (+ final norm, argmax) over residual row x (default: the decode
+// residual stream), then the step advance.
+static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = nullptr) {
     HeadArgs h{};
     h.w = s->out_w;
-    h.x = s->x;
+    h.x = x ? x : s->x;
     h.norm_w = s->out_norm;
     h.eps = s->cfg.rms_norm_eps;
     h.rows = s->tp.v;

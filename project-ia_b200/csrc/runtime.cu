@@ -358,6 +358,11 @@ void free_model(DevState* s) {
     s->chain_bar = nullptr;
     for (void* p : s->weight_allocs) cudaFree(p);
     s->weight_allocs.clear();
+    if (s->pf_base) cudaFree(s->pf_base);
+    if (s->pf_tok_host) cudaFreeHost(s->pf_tok_host);
+    s->pf_base = nullptr;
+    s->pf_tok_host = nullptr;
+    s->pf_cap = 0;
     s->qkv.clear();
     s->wo.clear();
     s->gu.clear();

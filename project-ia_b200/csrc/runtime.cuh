@@ -10,10 +10,13 @@
 #include <unordered_map>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "attn_decode.cuh"
 #include "gemv_q4.cuh"
 #include "head.cuh"
 #include "ops.cuh"
+#include "prefill.cuh"
 #include "qorus_b200.h"
 #include "tp.cuh"
 
@@ -150,6 +153,20 @@ struct DevState {
     unsigned long long* trace_buf = nullptr;   // [slots][4] device
     unsigned long long* tr_next = nullptr;     // capture cursor (null: untraced)
     uint32_t trace_slots = 0;
+    // prompt workspace (allocated on the first prompt of more than one row,
+    // grown when a longer prompt comes; never touched by decode steps)
+    uint32_t pf_cap = 0;           // rows the workspace holds
+    uint8_t* pf_base = nullptr;    // one allocation for all of it
+    uint32_t* pf_tok = nullptr;    // [cap] token ids
+    float* pf_x = nullptr;         // [cap][D] residual stream
+    __half* pf_act = nullptr;      // [2][cap][max(D, H)] activation halves
+    float* pf_tscale = nullptr;    // [cap]
+    float* pf_q = nullptr;         // [cap][d] rotated queries
+    float* pf_o = nullptr;         // [cap][d] attention output
+    float* pf_h = nullptr;         // [cap][h] SiLU(gate) * up
+    __half* pf_w = nullptr;        // [2][max M][max K] weight halves
+    float* pf_rscale = nullptr;    // [max M]
+    uint32_t* pf_tok_host = nullptr;  // pinned staging of the prompt ids
 };
 
 DevState* state_of(const q_context* ctx, bool create);
@@ -161,6 +178,12 @@ q_error_code ensure_graphs(q_context* ctx, DevState* s);
 q_error_code plan_attention(DevState* s);
 q_error_code capture_trace_graph(q_context* ctx, DevState* s);
 q_error_code check_device_status(const char* where);
+// Prompt of seq_len > 1 rows at positions pos.. through the tensor-core
+// prefill path (single-GPU contexts); leaves the last row's logits in
+// s->logits, its argmax in s->last_tok and the step scalars ready for the
+// next decode step.  Asynchronous on s->stream.
+q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t seq_len, uint32_t pos);
+PFN_cuTensorMapEncodeTiled tensor_map_encoder();
 // Reads and clears the device status word of the current device (0 = no
 // wait ran out); when it was set, re-zeroes every registered ticket area of
 // the device first.

@@ -135,6 +135,7 @@ _SIGS = {
     "q_b200_q4_pack": (_i, [_vp, _u32, _u32, _vp, _vp]),
     "q_b200_gemv_q4": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_gemv_q4_noalloc": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
+    "q_b200_gemm_q4": (_i, [_vp, _u32, _u32, _vp, _u32, _vp, _vp]),
     "q_b200_gemv_f32": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "q_b200_tp_unique_id": (_i, [_vp, _sz]),
     "q_b200_tp_init": (_i, [_vp, _u32, _u32, _vp, _sz]),
