@@ -180,7 +180,8 @@ static bool use_prefill(const DevState* s, uint32_t seq_len) {
 // One graph replay per row: rows 0..seq_len-2 run the layer stack only, the
 // last row also runs the LM head + argmax.  Row t sees the upstream softmax
 // row length N = pos + seq_len and unmasked positions 0..pos+t.
-static q_error_code run_rows(DevState* s, const uint32_t* tokens, uint32_t seq_len, uint32_t pos) {
+static q_error_code run_rows(DevState* s, const uint32_t* tokens, uint32_t seq_len, uint32_t pos,
+                             bool sample = false) {
     for (uint32_t t = 0; t < seq_len; ++t) {
         StepParams* hp = &s->h_step[t];
         hp->token = tokens[t];
@@ -189,7 +190,7 @@ static q_error_code run_rows(DevState* s, const uint32_t* tokens, uint32_t seq_l
         hp->valid = pos + t + 1;
         Q_CUDA(cudaMemcpyAsync(s->step, hp, sizeof *hp, cudaMemcpyHostToDevice, s->stream));
         const bool full = t + 1 == seq_len;
-        Q_CUDA(cudaGraphLaunch(full ? s->g_full : s->g_body, s->stream));
+        Q_CUDA(cudaGraphLaunch(full ? (sample ? s->g_sample : s->g_full) : s->g_body, s->stream));
         g_kernel_launches.fetch_add(full ? s->kernels_full : s->kernels_body);
     }
     return Q_OK;
@@ -224,24 +225,83 @@ q_error_code llama_forward(q_llama_model* model, q_context* ctx, const uint32_t*
     return check_device_status("llama_forward");
 }
 
+}  // extern "C"
+
+// Upstream keeps one xorshift64* state per host thread, seeded 123456789
+// (src/main.c:950-973); so does this library, and q_generate carries it to
+// the device for its loop and back.
+static thread_local unsigned long long t_rng_state = 123456789ULL;
+
+namespace {
+struct SampleOpWork {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+}  // namespace
+
+extern "C" {
+
 q_error_code q_sample_token(const float* logits, uint32_t vocab_size, float temperature,
                             uint32_t top_k, float top_p, uint32_t* token_id_out, q_context* ctx) {
-    (void)top_k;
-    (void)top_p;
     (void)ctx;
     if (!logits || !token_id_out) return Q_ERR_INVALID_ARG;
     if (vocab_size == 0) return Q_ERR_INVALID_SIZE;
     if (!(temperature >= 0.0f) || !std::isfinite(temperature)) return Q_ERR_INVALID_ARG;
-    if (temperature >= 1e-6f) return Q_ERR_INVALID_ARG;  // stochastic sampling: not in this build
-    // upstream main.c:870-881 on the caller's host logits
-    uint32_t bi = 0;
-    float bv = logits[0];
-    for (uint32_t i = 1; i < vocab_size; ++i)
-        if (logits[i] > bv) {
-            bv = logits[i];
-            bi = i;
-        }
-    *token_id_out = bi;
+    if (temperature < 1e-6f) {
+        // upstream main.c:870-881 on the caller's host logits
+        uint32_t bi = 0;
+        float bv = logits[0];
+        for (uint32_t i = 1; i < vocab_size; ++i)
+            if (logits[i] > bv) {
+                bv = logits[i];
+                bi = i;
+            }
+        *token_id_out = bi;
+        return Q_OK;
+    }
+    // temperature > 0: the device sampler on a copy of the caller's logits
+    static std::mutex mu;
+    static std::unordered_map<int, SampleOpWork> work;
+    std::lock_guard<std::mutex> lk(mu);
+    int dev = 0;
+    Q_CUDA(cudaGetDevice(&dev));
+    const size_t V = vocab_size, al = 256;
+    const size_t o_probs = (V * 4 + al - 1) / al * al, o_keep = o_probs + (V * 4 + al - 1) / al * al;
+    const size_t o_par = o_keep + (V + al - 1) / al * al, o_rng = o_par + al, o_key = o_rng + al, o_tok = o_key + al;
+    const size_t need = o_tok + al;
+    SampleOpWork& w = work[dev];
+    if (w.bytes < need) {
+        Q_CUDA(cudaDeviceSynchronize());
+        if (w.p) cudaFree(w.p);
+        w = SampleOpWork{};
+        if (!cuda_ok(cudaMalloc(&w.p, need), "cudaMalloc(sampler)")) return Q_ERR_ALLOC_FAILED;
+        w.bytes = need;
+    }
+    uint8_t* b = (uint8_t*)w.p;
+    SampleParams prm{temperature, top_k, top_p, 0u};
+    // upstream's SIMD path needs V >= 8 and a 32-byte aligned buffer; else its scalar fallback
+    prm.scalar_path = (vocab_size < 8 || ((uintptr_t)logits & 31)) ? 1u : 0u;
+    cudaStream_t st = op_stream();
+    Q_CUDA(cudaMemcpyAsync(b, logits, V * 4, cudaMemcpyHostToDevice, st));
+    Q_CUDA(cudaMemcpyAsync(b + o_par, &prm, sizeof prm, cudaMemcpyHostToDevice, st));
+    Q_CUDA(cudaMemcpyAsync(b + o_rng, &t_rng_state, 8, cudaMemcpyHostToDevice, st));
+    SampleArgs sa{};
+    sa.logits = (const float*)b;
+    sa.V = vocab_size;
+    sa.params = (const SampleParams*)(b + o_par);
+    sa.rng = (unsigned long long*)(b + o_rng);
+    sa.probs = (float*)(b + o_probs);
+    sa.keep = b + o_keep;
+    sa.best = (unsigned long long*)(b + o_key);
+    sa.token_out = (uint32_t*)(b + o_tok);
+    Q_CUDA(launch_ex(sample_kernel, dim3(1), dim3(SAMPLE_THREADS), 0, st, false, sa));
+    uint32_t tok = 0;
+    unsigned long long rs = 0;
+    Q_CUDA(cudaMemcpyAsync(&tok, b + o_tok, 4, cudaMemcpyDeviceToHost, st));
+    Q_CUDA(cudaMemcpyAsync(&rs, b + o_rng, 8, cudaMemcpyDeviceToHost, st));
+    Q_CUDA(cudaStreamSynchronize(st));
+    t_rng_state = rs;
+    *token_id_out = tok;
     return Q_OK;
 }
 
@@ -254,7 +314,6 @@ q_error_code q_generate(q_generation_state* st) {
     if (!(st->temperature >= 0.0f) || !std::isfinite(st->temperature)) return Q_ERR_INVALID_ARG;
     if (!st->tokenizer->initialized) return Q_ERR_INVALID_ARG;
     if (!st->ctx->scratch_buffer || !st->ctx->kv_buffer) return Q_ERR_INVALID_ARG;
-    if (st->temperature >= 1e-6f) return Q_ERR_INVALID_ARG;  // greedy only in this build
     const q_llama_config& c = st->model->config;
     if (st->num_prompt_tokens > c.max_seq_len) return Q_ERR_INVALID_SIZE;
     for (uint32_t t = 0; t < st->num_prompt_tokens; ++t)
@@ -266,10 +325,25 @@ q_error_code q_generate(q_generation_state* st) {
     q_error_code rc = ready(st->model, st->ctx, &s);
     if (rc != Q_OK) return rc;
     Q_CUDA(cudaStreamSynchronize(s->stream));
+    // temperature > 0: every token is drawn on the device by the sampler
+    // (upstream q_sample_token per step, main.c:1044 and 1109) from this
+    // thread's xorshift state, carried to the device and back
+    const bool sample = st->temperature >= 1e-6f;
+    if (sample) {
+        if (s->tp_world != 1) return Q_ERR_INVALID_ARG;  // sampling needs one rank's whole vocabulary
+        if ((rc = ensure_sample_graph(st->ctx, s)) != Q_OK) return rc;
+        const SampleParams prm{st->temperature, st->top_k, st->top_p, 0u};
+        Q_CUDA(cudaMemcpy(s->samp, &prm, sizeof prm, cudaMemcpyHostToDevice));
+        Q_CUDA(cudaMemcpy(s->rng, &t_rng_state, 8, cudaMemcpyHostToDevice));
+    }
+    // a forward is followed by a draw only when the loop below will take a
+    // token from it (upstream draws inside the loop), so the thread's
+    // random stream advances exactly as upstream's would
+    const bool draw0 = sample && st->num_prompt_tokens < c.max_seq_len;
     if (use_prefill(s, st->num_prompt_tokens))
-        rc = run_prefill(s, (float*)st->ctx->kv_buffer, st->prompt_tokens, st->num_prompt_tokens, 0);
+        rc = run_prefill(s, (float*)st->ctx->kv_buffer, st->prompt_tokens, st->num_prompt_tokens, 0, draw0);
     else
-        rc = run_rows(s, st->prompt_tokens, st->num_prompt_tokens, 0);
+        rc = run_rows(s, st->prompt_tokens, st->num_prompt_tokens, 0, draw0);
     if (rc != Q_OK) return rc;
     st->current_pos = st->num_prompt_tokens;
     while (st->num_generated_tokens < st->max_tokens) {
@@ -282,10 +356,12 @@ q_error_code q_generate(q_generation_state* st) {
         st->generated_tokens[st->num_generated_tokens++] = tok;
         if (tok == st->tokenizer->eos_token_id) break;
         q_arena_reset(st->ctx);
-        if ((rc = run_rows(s, &tok, 1, st->current_pos)) != Q_OK) return rc;
+        const bool draw = sample && st->num_generated_tokens < st->max_tokens && st->current_pos + 1 < c.max_seq_len;
+        if ((rc = run_rows(s, &tok, 1, st->current_pos, draw)) != Q_OK) return rc;
         st->current_pos++;
     }
     Q_CUDA(cudaStreamSynchronize(s->stream));
+    if (sample) Q_CUDA(cudaMemcpy(&t_rng_state, s->rng, 8, cudaMemcpyDeviceToHost));
     return check_device_status("q_generate");
 }
 

@@ -210,8 +210,10 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     s->tok_out = (uint32_t*)dev_arena_alloc(s, (size_t)s->tok_cap * 4);
     s->tok_count = (uint32_t*)dev_arena_alloc(s, 4);
     s->last_tok = (uint32_t*)dev_arena_alloc(s, 4);
+    s->samp = (SampleParams*)dev_arena_alloc(s, sizeof(SampleParams));
+    s->rng = (unsigned long long*)dev_arena_alloc(s, 8);
     if (!s->x || !s->q || !s->att || !s->h || !s->logits || !s->best || !s->step || !s->tok_out ||
-        !s->tok_count || !s->last_tok || !s->chain_bar) {
+        !s->tok_count || !s->last_tok || !s->chain_bar || !s->samp || !s->rng) {
         free_model(s);
         return Q_ERR_ARENA_OOM;
     }
@@ -522,8 +524,10 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
 }
 
 // LM head (+ final norm, argmax) over residual row x (default: the decode
-// residual stream), then the step advance.
-static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = nullptr) {
+// residual stream), optionally the sampler (which replaces the argmax key
+// with a drawn token when the context's temperature is above 0), then the
+// step advance.
+static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = nullptr, bool sample = false) {
     HeadArgs h{};
     h.w = s->out_w;
     h.x = x ? x : s->x;
@@ -555,6 +559,19 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
         e = nccl_status(n->all_reduce(s->best, s->best, 1, ncclUint64, ncclMax, s->comm, st));
         if (e != cudaSuccess) return e;
     }
+    if (sample) {
+        if (s->tp_world != 1) return cudaErrorInvalidValue;  // the sampler needs the whole vocabulary
+        SampleArgs sa{};
+        sa.logits = s->logits;
+        sa.V = s->cfg.vocab_size;
+        sa.params = s->samp;
+        sa.rng = s->rng;
+        sa.probs = s->samp_probs;
+        sa.keep = s->samp_keep;
+        sa.best = s->best;
+        e = launch_ex(sample_kernel, dim3(1), dim3(SAMPLE_THREADS), 0, st, true, sa);
+        if (e != cudaSuccess) return e;
+    }
     AdvanceArgs a{};
     a.step = s->step;
     a.best = s->best;
@@ -567,14 +584,14 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
 }
 
 static q_error_code capture(DevState* s, float* kv, bool with_head, cudaGraphExec_t* out,
-                            uint64_t* n_kernels) {
+                            uint64_t* n_kernels, bool sample = false) {
     cudaStream_t st = s->stream;
     cudaGraph_t g = nullptr;
     const uint64_t before = g_kernel_launches.load();
     if (!cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture"))
         return Q_ERR_INVALID_ARG;
     cudaError_t e = enqueue_layers(s, kv, st);
-    if (e == cudaSuccess && with_head) e = enqueue_head(s, st);
+    if (e == cudaSuccess && with_head) e = enqueue_head(s, st, nullptr, sample);
     cudaError_t e2 = cudaStreamEndCapture(st, &g);
     *n_kernels = g_kernel_launches.load() - before;
     g_kernel_launches.fetch_sub(*n_kernels);  // captured, not launched
@@ -602,12 +619,34 @@ q_error_code capture_trace_graph(q_context* ctx, DevState* s) {
     return rc;
 }
 
+// The sampler's scratch ([V] probabilities and keep flags) is allocated on
+// the first sampled generation, not at build time, so greedy-only callers
+// never pay for it.
+q_error_code ensure_sample_scratch(DevState* s) {
+    if (s->samp_probs) return Q_OK;
+    const size_t V = s->cfg.vocab_size;
+    void* p = nullptr;
+    if (!cuda_ok(cudaMalloc(&p, V * 5 + 256), "cudaMalloc(sampler scratch)")) return Q_ERR_ALLOC_FAILED;
+    s->samp_probs = (float*)p;
+    s->samp_keep = (uint8_t*)p + (V * 4 + 255) / 256 * 256;
+    return Q_OK;
+}
+
+q_error_code ensure_sample_graph(q_context* ctx, DevState* s) {
+    if (s->g_sample) return Q_OK;
+    q_error_code rc = ensure_sample_scratch(s);
+    if (rc != Q_OK) return rc;
+    uint64_t nk = 0;
+    return capture(s, (float*)ctx->kv_buffer, true, &s->g_sample, &nk, true);
+}
+
 q_error_code ensure_graphs(q_context* ctx, DevState* s) {
     if (s->g_full && s->graph_kv == ctx->kv_buffer) return Q_OK;
     if (s->g_body) cudaGraphExecDestroy(s->g_body);
     if (s->g_full) cudaGraphExecDestroy(s->g_full);
     if (s->g_trace) cudaGraphExecDestroy(s->g_trace);
-    s->g_body = s->g_full = s->g_trace = nullptr;
+    if (s->g_sample) cudaGraphExecDestroy(s->g_sample);
+    s->g_body = s->g_full = s->g_trace = s->g_sample = nullptr;
     float* kv = (float*)ctx->kv_buffer;
     q_error_code rc = make_kv_map(s, kv);
     if (rc == Q_OK) rc = capture(s, kv, false, &s->g_body, &s->kernels_body);

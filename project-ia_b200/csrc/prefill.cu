@@ -156,7 +156,7 @@ static cudaError_t launch_pf_attention(DevState* s, float* kv, uint32_t layer, u
     return cudaLaunchKernel(kern, grid, dim3(PF_ATT_THREADS), params, smem, st);
 }
 
-q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t S, uint32_t pos) {
+q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t S, uint32_t pos, bool sample) {
     const q_llama_config& c = s->cfg;
     const TpShape& t = s->tp;
     if (s->tp_world != 1) return Q_ERR_INVALID_ARG;
@@ -254,7 +254,7 @@ q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_
     hp->n_row = pos + S;
     hp->valid = pos + S;
     Q_CUDA(cudaMemcpyAsync(s->step, hp, sizeof *hp, cudaMemcpyHostToDevice, st));
-    Q_CUDA(enqueue_head(s, st, s->pf_x + (size_t)(S - 1) * D));
+    Q_CUDA(enqueue_head(s, st, s->pf_x + (size_t)(S - 1) * D, sample));
     return Q_OK;
 }
 

@@ -348,6 +348,8 @@ void free_model(DevState* s) {
     if (s->g_body) cudaGraphExecDestroy(s->g_body);
     if (s->g_full) cudaGraphExecDestroy(s->g_full);
     if (s->g_trace) cudaGraphExecDestroy(s->g_trace);
+    if (s->g_sample) cudaGraphExecDestroy(s->g_sample);
+    s->g_sample = nullptr;
     if (s->trace_buf) cudaFree(s->trace_buf);
     s->trace_buf = nullptr;
     s->g_body = s->g_full = s->g_trace = nullptr;
@@ -360,6 +362,9 @@ void free_model(DevState* s) {
     s->weight_allocs.clear();
     if (s->pf_base) cudaFree(s->pf_base);
     if (s->pf_tok_host) cudaFreeHost(s->pf_tok_host);
+    if (s->samp_probs) cudaFree(s->samp_probs);
+    s->samp_probs = nullptr;
+    s->samp_keep = nullptr;
     s->pf_base = nullptr;
     s->pf_tok_host = nullptr;
     s->pf_cap = 0;

@@ -17,6 +17,7 @@
 #include "head.cuh"
 #include "ops.cuh"
 #include "prefill.cuh"
+#include "sample.cuh"
 #include "qorus_b200.h"
 #include "tp.cuh"
 
@@ -144,6 +145,12 @@ struct DevState {
     uint32_t *tok_out = nullptr, *tok_count = nullptr, *last_tok = nullptr;
     uint32_t tok_cap = 0;
     StepParams* h_step = nullptr;  // pinned, one per row of a call
+    // sampling (temperature > 0): parameters, xorshift state, scratch [V]
+    SampleParams* samp = nullptr;
+    unsigned long long* rng = nullptr;
+    float* samp_probs = nullptr;
+    uint8_t* samp_keep = nullptr;
+    cudaGraphExec_t g_sample = nullptr;  // layers + head + sampler + advance
     // captured graphs (valid for graph_kv)
     void* graph_kv = nullptr;
     cudaGraphExec_t g_body = nullptr, g_full = nullptr;
@@ -175,6 +182,8 @@ void* dev_arena_alloc(DevState* s, size_t bytes);
 
 q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* model);
 q_error_code ensure_graphs(q_context* ctx, DevState* s);
+q_error_code ensure_sample_graph(q_context* ctx, DevState* s);
+q_error_code ensure_sample_scratch(DevState* s);
 q_error_code plan_attention(DevState* s);
 q_error_code capture_trace_graph(q_context* ctx, DevState* s);
 q_error_code check_device_status(const char* where);
@@ -182,7 +191,8 @@ q_error_code check_device_status(const char* where);
 // prefill path (single-GPU contexts); leaves the last row's logits in
 // s->logits, its argmax in s->last_tok and the step scalars ready for the
 // next decode step.  Asynchronous on s->stream.
-q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t seq_len, uint32_t pos);
+q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t seq_len, uint32_t pos,
+                         bool sample = false);
 PFN_cuTensorMapEncodeTiled tensor_map_encoder();
 // Reads and clears the device status word of the current device (0 = no
 // wait ran out); when it was set, re-zeroes every registered ticket area of
