@@ -82,7 +82,9 @@ static bool halves_map(CUtensorMap* m, const __half* base, uint32_t rows, uint32
 
 static cudaError_t launch_act_split(DevState* s, const ActSplitArgs& a, uint32_t S, cudaStream_t st) {
     const size_t smem = (size_t)a.K * 4;
-    cudaError_t e = ensure_smem_attr((const void*)act_split_kernel, (int)std::max<size_t>(smem, 48 * 1024));
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    // one attribute per kernel and device: the opt-in maximum covers every K
+    cudaError_t e = ensure_smem_attr((const void*)act_split_kernel, 227 * 1024);
     if (e != cudaSuccess) return e;
     (void)s;
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
