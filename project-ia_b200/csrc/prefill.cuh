@@ -37,14 +37,22 @@ namespace qb200 {
 
 // ---- tile shape -------------------------------------------------------------------
 static constexpr uint32_t PF_BM = 128;  // token rows per tile (MMA M = TMEM lanes)
-static constexpr uint32_t PF_BN = 256;  // weight rows per tile (MMA N = accumulator columns)
+static constexpr uint32_t PF_BN = 128;  // weight rows per tile (MMA N = accumulator columns)
 static constexpr uint32_t PF_BK = 64;   // fp16 per K chunk: one 128-byte swizzle row
-static constexpr uint32_t PF_STAGES = 2;
+static constexpr uint32_t PF_STAGES = 3;
 static constexpr uint32_t PF_A_BYTES = PF_BM * PF_BK * 2;                    // 16 KB
-static constexpr uint32_t PF_B_BYTES = PF_BN * PF_BK * 2;                    // 32 KB
+static constexpr uint32_t PF_B_BYTES = PF_BN * PF_BK * 2;                    // 16 KB
 static constexpr uint32_t PF_STAGE_BYTES = 2 * PF_A_BYTES + 2 * PF_B_BYTES;  // hi + lo of each
 static constexpr uint32_t PF_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-static constexpr uint32_t PF_TMEM_COLS = 2 * PF_BN;  // two accumulator buffers
+// The tensor core adds each MMA's products into its fp32 accumulator with
+// truncation to the accumulator's precision, so the error grows with the
+// number of MMAs per accumulation (measured: 3e-4 relative at K = 14336 in
+// one accumulator).  So the MMAs accumulate PF_SEG K chunks (48 MMAs) into
+// one of two partial buffers and the epilogue warps add each partial, in
+// correctly rounded fp32, into a running sum kept in TMEM:
+// columns [0, N) and [N, 2N) partials, [2N, 3N) the running sum.
+static constexpr uint32_t PF_SEG = 4;
+static constexpr uint32_t PF_TMEM_COLS = 512;
 static constexpr size_t PF_SMEM = (size_t)PF_STAGES * PF_STAGE_BYTES + 1024 /*align*/ + 256;
 
 // fp16 range scaling: a row is multiplied by 2^e with e chosen so its largest
@@ -254,6 +262,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d_pf(void* dst_smem, const CUtensorMap* map, int x, int y, int z,
                                                uint64_t* bar) {
     asm volatile(
@@ -346,12 +374,14 @@ __device__ __forceinline__ void pf_epilogue32(const PfGemmArgs& a, uint32_t tok,
 // Persistent: CTA c takes tiles c, c + grid, ...; tile t = (weight tile
 // t / n_mt, token tile t % n_mt), so CTAs running at once share weight tiles
 // (read from HBM once, then from L2).  Roles: warp 0 lane 0 issues the TMA
-// loads of a 2-stage ring (A_hi, A_lo, B_hi, B_lo per stage); warp 1 owns
-// TMEM (512 columns: two 128 x 256 fp32 accumulators) and its lane 0 issues
-// the MMAs; warps 2..5 drain an accumulator (TMEM lanes 32 (w % 4) + i) into
-// the epilogue while the next tile accumulates into the other.  Every wait
-// is bounded; a role that gives up records the code and stops, the others
-// then time out too, and the MMA issuer drains its MMAs before TMEM is freed.
+// loads of a 3-stage ring (A_hi, A_lo, B_hi, B_lo per stage); warp 1 owns
+// TMEM and its lane 0 issues the MMAs, PF_SEG K chunks per partial buffer
+// (alternating between two, so the MMAs run on while the previous partial is
+// folded); warps 2..5 (TMEM lanes 32 (w % 4) + i) fold each partial into the
+// running sum and, after a tile's last partial, run the epilogue.  Every
+// wait is bounded; a role that gives up records the code and stops, the
+// others then time out too, and the MMA issuer drains its MMAs before TMEM
+// is freed.
 __global__ void __launch_bounds__(PF_THREADS, 1)
     pf_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const PfGemmArgs a) {
@@ -360,14 +390,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     uint8_t* smem = pf_smem_raw + (base - smem_u32(pf_smem_raw));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + PF_STAGES * PF_STAGE_BYTES);
     uint64_t* empty = full + PF_STAGES;
-    uint64_t* acc_full = empty + PF_STAGES;
-    uint64_t* acc_empty = acc_full + 2;
-    uint64_t* drain = acc_empty + 2;
+    uint64_t* pfull = empty + PF_STAGES;
+    uint64_t* pfree = pfull + 2;
+    uint64_t* drain = pfree + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n_tiles = a.n_mt * a.n_nt;
     const uint32_t nk = (a.K + PF_BK - 1) / PF_BK;
+    const uint32_t nseg = (nk + PF_SEG - 1) / PF_SEG;
 
     if (tid == 0) {
         for (uint32_t s = 0; s < PF_STAGES; ++s) {
@@ -375,8 +406,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&pfull[b], 1);
+            mbar_init(&pfree[b], 4);
         }
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -435,22 +466,24 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---- MMA issuer ----
-            uint32_t s = 0, ph = 0, it = 0;
+            uint32_t s = 0, ph = 0, g = 0;  // ring slot, parity, partials started
             bool ok = true;
-            for (uint32_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++it) {
-                const uint32_t ab = it & 1;
-                if (it >= 2 && !mbar_wait(&acc_empty[ab], ((it >> 1) - 1) & 1, QDEV_WAIT_EMPTY_TIMEOUT)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem + ab * PF_BN;
-                for (uint32_t kc = 0; kc < nk; ++kc) {
+            for (uint32_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                for (uint32_t kc = 0; kc < nk && ok; ++kc) {
+                    const uint32_t buf = g & 1;
+                    if (kc % PF_SEG == 0) {
+                        if (g >= 2 && !mbar_wait(&pfree[buf], ((g >> 1) - 1) & 1, QDEV_WAIT_EMPTY_TIMEOUT)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
                     if (!mbar_wait(&full[s], ph, QDEV_WAIT_FULL_TIMEOUT)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
+                    const uint32_t d = tmem + buf * PF_BN;
                     const uint32_t st = base + s * PF_STAGE_BYTES;
 #pragma unroll
                     for (uint32_t kk = 0; kk < PF_BK / 16; ++kk) {
@@ -458,7 +491,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                         const uint64_t alo = umma_desc_sw128(st + PF_A_BYTES + kk * 32);
                         const uint64_t bhi = umma_desc_sw128(st + 2 * PF_A_BYTES + kk * 32);
                         const uint64_t blo = umma_desc_sw128(st + 2 * PF_A_BYTES + PF_B_BYTES + kk * 32);
-                        umma_f16(d, ahi, bhi, (kc | kk) != 0);
+                        umma_f16(d, ahi, bhi, ((kc % PF_SEG) | kk) != 0);
                         umma_f16(d, ahi, blo, 1);
                         umma_f16(d, alo, bhi, 1);
                     }
@@ -467,34 +500,53 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                         s = 0;
                         ph ^= 1;
                     }
+                    if (kc % PF_SEG == PF_SEG - 1 || kc == nk - 1) {
+                        umma_commit(&pfull[buf]);  // this partial is complete
+                        ++g;
+                    }
                 }
-                if (ok) umma_commit(&acc_full[ab]);
             }
             // every MMA issued has finished before TMEM can be freed
             umma_commit(drain);
             mbar_wait(drain, 0, QDEV_WAIT_FULL_TIMEOUT);
         }
     } else {
-        // ---- epilogue: warps 2..5, TMEM lane quarter warp % 4 ----
+        // ---- fold + epilogue: warps 2..5, TMEM lane quarter warp % 4 ----
         const uint32_t quarter = warp & 3;
-        uint32_t it = 0;
-        for (uint32_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
-            const uint32_t ab = it & 1;
-            if (!mbar_wait(&acc_full[ab], (it >> 1) & 1, QDEV_WAIT_FULL_TIMEOUT)) break;
-            tc_fence_after();
+        const uint32_t lanes = (quarter * 32u) << 16;
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
             const uint32_t mt = t % a.n_mt, nt = t / a.n_mt;
             const uint32_t tok = mt * PF_BM + quarter * 32 + lane;
             const float tsc = tok < a.S ? __ldg(a.tscale + tok) : 0.0f;
-            const uint32_t taddr = tmem + ((quarter * 32u) << 16) + ab * PF_BN;
+            for (uint32_t sg = 0; sg < nseg; ++sg, ++g) {
+                const uint32_t buf = g & 1;
+                if (!mbar_wait(&pfull[buf], (g >> 1) & 1, QDEV_WAIT_FULL_TIMEOUT)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t pa = tmem + lanes + buf * PF_BN, ra = tmem + lanes + 2 * PF_BN;
 #pragma unroll 1
-            for (uint32_t c = 0; c < PF_BN / 32; ++c) {
-                float v[32];
-                tmem_ld32(taddr + c * 32, v);
-                pf_epilogue32(a, tok, nt * PF_BN + c * 32, tsc, v);
+                for (uint32_t c = 0; c < PF_BN / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(pa + c * 32, v);
+                    if (sg > 0) {
+                        float r[32];
+                        tmem_ld32(ra + c * 32, r);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(r[i], v[i]);
+                    }
+                    if (sg + 1 < nseg)
+                        tmem_st32(ra + c * 32, v);
+                    else
+                        pf_epilogue32(a, tok, nt * PF_BN + c * 32, tsc, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pfree[buf]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[ab]);
         }
     }
     tc_fence_before();
