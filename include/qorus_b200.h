@@ -93,6 +93,36 @@ q_error_code q_b200_profile_step(q_llama_model* model, q_context* ctx, uint32_t 
 /* Device logits of the last forward / decode step ([vocab] fp32). */
 const float* q_b200_device_logits(q_context* ctx);
 
+/* ---- batched decode (several sequences per step) -----------------------
+ * Upstream decodes one sequence per llama_forward call (qorus.h:212-219,
+ * src/main.c:994-1131).  These calls decode up to 16 sequences together,
+ * every weight streamed from HBM once per step for all of them.  Sequence b
+ * has its own KV cache in the upstream layout [L][n_kv][max_seq][K|V]
+ * (allocated by q_b200_batch_init, beside ctx's single-sequence cache).
+ * Single-GPU contexts, after llama_build_graph. */
+
+/* Allocate the B caches (zeroed) and step state, capture the batched step. */
+q_error_code q_b200_batch_init(q_context* ctx, q_llama_model* model, uint32_t batch);
+
+/* Copy bytes between a host buffer and sequence seq's cache (byte offset
+ * into its upstream layout). */
+q_error_code q_b200_batch_kv_write(q_context* ctx, uint32_t seq, size_t offset, const void* host,
+                                   size_t bytes);
+q_error_code q_b200_batch_kv_read(q_context* ctx, uint32_t seq, size_t offset, void* host, size_t bytes);
+
+/* One greedy step of every sequence: token tokens[b] at position pos[b]
+ * (attending to its cache positions 0..pos[b]).  logits (host, [B][vocab])
+ * and next_tokens (host, [B], the argmax) may each be NULL. */
+q_error_code q_b200_decode_batch(q_llama_model* model, q_context* ctx, const uint32_t* tokens,
+                                 const uint32_t* pos, float* logits, uint32_t* next_tokens);
+
+/* n_steps greedy steps from tokens / pos, each sequence's argmax fed back on
+ * the device (graph replay); out_tokens[i * B + b] (host) receives step i's
+ * token of sequence b.  Asynchronous unless sync != 0 (out_tokens written
+ * only then). */
+q_error_code q_b200_decode_batch_loop(q_llama_model* model, q_context* ctx, const uint32_t* tokens,
+                                      const uint32_t* pos, uint32_t n_steps, uint32_t* out_tokens, int sync);
+
 /* ---- tensor parallelism over the GPUs of one node ----------------------
  * No counterpart upstream (upstream is single-process).  One process per
  * GPU: rank 0 calls q_b200_tp_unique_id and shares the 128 bytes with the

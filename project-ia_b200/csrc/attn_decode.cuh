@@ -64,6 +64,10 @@ struct AttnArgs {
     uint32_t slots;          // ring depth (2..ATT_MAX_SLOTS)
     float scale;             // 1/sqrtf(hd), computed on the host like upstream
     unsigned long long* trace;  // step-trace slot (null: off)
+    // batched decode (grid z = sequence b): q, out and step advance by these
+    // per sequence, and sequence b's cache planes follow the first b caches
+    uint32_t seq_stride;     // floats of q / out per sequence
+    uint32_t n_layers;       // planes per sequence = n_layers * n_kv_heads
 };
 
 // ring[slots][16 KB] | sc[G][chunk_alloc] | ored[PG][G][hd]
@@ -150,12 +154,16 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     pdl_trigger();
     // Step scalars come from the previous graph replay or a host copy, both
     // complete before this grid starts.
-    const uint32_t valid = a.step->valid, N = a.step->n_row, cur = a.step->pos;
+    const uint32_t bz = blockIdx.z;  // sequence (batched decode; 0 otherwise)
+    const StepParams* stp = a.step + bz;
+    const uint32_t valid = stp->valid, N = stp->n_row, cur = stp->pos;
     // CTA r takes whole ring stages [n_st r / CS, n_st (r+1) / CS) of the
     // valid rows, so only the last stage of the sequence is a partial box
     const uint32_t n_st = (valid + SP - 1) / SP;
     const uint32_t p0 = min(n_st * r / CS * SP, valid), p1 = min(n_st * (r + 1) / CS * SP, valid);
-    const int plane = (int)(a.layer * a.n_kv_heads + h);
+    const int plane = (int)(((size_t)bz * a.n_layers + a.layer) * a.n_kv_heads + h);
+    const float* qseq = a.q + (size_t)bz * a.seq_stride;
+    float* oseq = a.out + (size_t)bz * a.seq_stride;
 
     if (warp == NW) {
         // ---- producer: K rows of the chunk, then its V rows ------------------
@@ -211,7 +219,7 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
         for (int g = 0; g < G; ++g)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                qr[g][i] = reinterpret_cast<const float4*>(a.q + (size_t)(h * G + g) * HD)[sub + i * LPP];
+                qr[g][i] = reinterpret_cast<const float4*>(qseq + (size_t)(h * G + g) * HD)[sub + i * LPP];
         float mx[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) mx[g] = -INFINITY;
@@ -363,7 +371,7 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
         for (uint32_t k = tid; k < per; k += T) {
             float acc = 0.0f;
             for (uint32_t rr = 0; rr < CS; ++rr) acc += pgath[rr * per + k];
-            a.out[(size_t)h * G * HD + o0 + k] = __fmul_rn(acc, linv[(o0 + k) / HD]);
+            oseq[(size_t)h * G * HD + o0 + k] = __fmul_rn(acc, linv[(o0 + k) / HD]);
         }
     }
     // (no shared memory of another CTA is touched after the second barrier)

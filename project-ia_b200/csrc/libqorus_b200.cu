@@ -5,6 +5,7 @@
 #include "tp.cu"
 #include "model.cu"
 #include "prefill.cu"
+#include "batch.cu"
 #include "api.cu"
 #include "api_model.cu"
 #include "api_ops.cu"

@@ -345,6 +345,7 @@ void* dev_arena_alloc(DevState* s, size_t bytes) {
 }
 
 void free_model(DevState* s) {
+    free_batch(s);
     if (s->g_body) cudaGraphExecDestroy(s->g_body);
     if (s->g_full) cudaGraphExecDestroy(s->g_full);
     if (s->g_trace) cudaGraphExecDestroy(s->g_trace);

@@ -18,6 +18,7 @@
 #include "ops.cuh"
 #include "prefill.cuh"
 #include "sample.cuh"
+#include "batch.cuh"
 #include "qorus_b200.h"
 #include "tp.cuh"
 
@@ -98,6 +99,27 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
     return cudaLaunchKernelEx(&cfg, kernel, args);
 }
 
+// ---- batched decode state (q_b200_batch_init) -------------------------------------
+
+struct BatchState {
+    uint32_t B = 0, TG = 0;        // sequences, groups of 8 in the fragment table
+    float* kv = nullptr;           // [B] caches, each [L][n_kv][max_seq][K|V]
+    size_t kv_bytes_seq = 0;
+    CUtensorMap kv_map;            // attention view: planes (b * L + layer) * n_kv + head
+    uint8_t* base = nullptr;       // one allocation for the buffers below
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    uint32_t* frag = nullptr;      // input fragments of the next GEMV
+    float* tscale = nullptr;
+    StepParams* step = nullptr;    // [B]
+    unsigned long long* best = nullptr;
+    uint32_t *tok_out = nullptr, *tok_count = nullptr;
+    uint32_t tok_cap = 0;
+    StepParams* h_step = nullptr;  // pinned [B]
+    float wmul = 1.0f, wdiv = 1.0f;  // LM head scale
+    cudaGraphExec_t graph = nullptr;
+    uint64_t kernels = 0;
+};
+
 // ---- per-context device state ----------------------------------------------------
 
 struct DevState {
@@ -151,6 +173,7 @@ struct DevState {
     float* samp_probs = nullptr;
     uint8_t* samp_keep = nullptr;
     cudaGraphExec_t g_sample = nullptr;  // layers + head + sampler + advance
+    BatchState batch;
     // captured graphs (valid for graph_kv)
     void* graph_kv = nullptr;
     cudaGraphExec_t g_body = nullptr, g_full = nullptr;
@@ -205,5 +228,6 @@ void unregister_zero_area(void* p);
 cudaError_t tp_allreduce(DevState* s, void* data, uint32_t n, int op, cudaStream_t st,
                          float* out = nullptr);
 void free_model(DevState* s);
+void free_batch(DevState* s);
 
 }  // namespace qb200

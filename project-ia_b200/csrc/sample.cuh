@@ -176,10 +176,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS, 1) sample_kernel(const SampleA
     // per-thread contiguous ranges for the order-dependent steps
     const uint32_t chunk = (V + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
     const uint32_t c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
-    bool filtered = false;
     // ---- top-k ----
     if (prm.top_k > 0 && prm.top_k < V) {
-        filtered = true;
         uint32_t n_gt = 0;
         const uint32_t key = radix_kth_largest(p, nullptr, V, prm.top_k, hist, &n_gt);
         const uint32_t m = prm.top_k - n_gt;  // ties at the threshold, lowest index first
@@ -201,7 +199,6 @@ __global__ void __launch_bounds__(SAMPLE_THREADS, 1) sample_kernel(const SampleA
     }
     // ---- top-p ----
     if (prm.top_p > 0.0f && prm.top_p < 1.0f) {
-        filtered = true;
         const double fx = 4503599627370496.0;  // 2^52
         const unsigned long long target = (unsigned long long)((double)prm.top_p * fx);
         uint32_t prefix = 0, mask = 0;
@@ -275,7 +272,6 @@ __global__ void __launch_bounds__(SAMPLE_THREADS, 1) sample_kernel(const SampleA
         for (uint32_t i = c0; i < c1; ++i) p[i] = a.keep[i] && s > 0.0f ? __fdiv_rn(p[i], s) : (s > 0.0f ? 0.0f : p[i]);
         __syncthreads();
     }
-    (void)filtered;
     // ---- the draw (upstream xorshift64*, one per call) ----
     __shared__ float s_r;
     if (tid == 0) {

@@ -131,6 +131,11 @@ _SIGS = {
     "q_b200_decode_loop": (_i, [_vp, _vp, _u32, _u32, _u32, _vp, _i]),
     "q_b200_profile_step": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
     "q_b200_device_logits": (_vp, [_vp]),
+    "q_b200_batch_init": (_i, [_vp, _vp, _u32]),
+    "q_b200_batch_kv_write": (_i, [_vp, _u32, _sz, _vp, _sz]),
+    "q_b200_batch_kv_read": (_i, [_vp, _u32, _sz, _vp, _sz]),
+    "q_b200_decode_batch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "q_b200_decode_batch_loop": (_i, [_vp, _vp, _vp, _vp, _u32, _vp, _i]),
     "q_b200_q4_packed_bytes": (_sz, [_u32, _u32]),
     "q_b200_q4_pack": (_i, [_vp, _u32, _u32, _vp, _vp]),
     "q_b200_gemv_q4": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
