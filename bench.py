@@ -280,6 +280,44 @@ def gemv_sweep(Q, torch, peak_gbs: float, host: bool) -> list:
     return out
 
 
+def prefill_measure(Q, m, torch, peak_tf: float, reps: int = 3) -> dict:
+    """one prompt of 2048 seeded uniform ids in
+    [0, 128256) through llama_forward (the tensor-core prompt path), host
+    ids in and the last row's logits out.  TTFT = wall time of the call;
+    device time = CUDA events on the library stream around the same call.
+    One untimed call first (workspace allocation, first-use set-up)."""
+    S = PREFILL
+    toks = np.zeros(S, np.uint32)
+    Q.lib.q_b200_fill_tokens(Q.ptr(toks), S, SEED, 9, 0, CFG8B["vocab"])
+    stream = torch.cuda.ExternalStream(m.stream)
+    m.forward(toks, 0)
+    walls, devs = [], []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0.record(stream)
+        m.forward(toks, 0)
+        e1.record(stream)
+        walls.append(time.perf_counter() - t0)
+        torch.cuda.synchronize()
+        devs.append(e0.elapsed_time(e1) * 1e-3)
+    D, H, L = CFG8B["dim"], CFG8B["hidden"], CFG8B["layers"]
+    kvd = CFG8B["kv_heads"] * (D // CFG8B["heads"])
+    lin = L * (D * D * 2 + kvd * D * 2 + H * D * 3)
+    flop = 2.0 * lin * S + 2.0 * D * CFG8B["vocab"]  # projections + the last row's head
+    attn = L * 2.0 * 2 * D * (S * (S + 1) / 2)          # causal q.k and p.v
+    ttft = min(walls)
+    dev = min(devs)
+    return {"tokens": S, "ttft_ms": round(ttft * 1e3, 2), "device_ms": round(dev * 1e3, 2),
+            "prompt_tok_s": round(S / ttft, 1), "flop": flop + attn,
+            "tflops": round((flop + attn) / dev / 1e12, 1),
+            "frac_of_bf16_peak": round((flop + attn) / dev / 1e12 / peak_tf, 4),
+            "note": "the projections run 3 fp16 MMAs (hi*hi, hi*lo, lo*hi) per product for fp32-grade "
+                    "results, so tensor-pipe work is 3x the flop counted here",
+            "reps": reps, "source": "llama_forward(2048 ids, pos 0) with host buffers"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -287,7 +325,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["gemv", "attention", "head"],
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--only", choices=["gemv", "attention", "head", "prefill"],
                     help="profiling runs: the gate/up GEMV alone, a few decode steps of a "
                          "2-layer 8B-shaped model (small vocab) over a 2048-position cache, "
                          "or the FP32 LM-head GEMV (128256 x 4096) alone")
@@ -351,6 +390,19 @@ def main():
         us = e0.elapsed_time(e1) * 1e3 / (n - 2)
         print(json.dumps({"only": "head", "launches": n, "us_per_launch": round(us, 1),
                           "gbs": round(M * K * 4 / (us * 1e-6) / 1e9, 1)}), flush=True)
+        return
+    if args.only == "prefill":
+        # profiling run: a 2048-row prompt through 2 Llama-3-8B-shaped layers
+        import qorus_b200 as Q
+        small = Q.config(32000, CFG8B["dim"], CFG8B["hidden"], 2, CFG8B["heads"], CFG8B["kv_heads"], 2304)
+        spath = str(Path(model_path(2304)).with_name("qorus_llama3_8b_2layer_prefill.qorus"))
+        Q.write_model(spath, small, seed=SEED, threads=0)
+        ms = Q.Model(spath)
+        toks = np.zeros(PREFILL, np.uint32)
+        Q.lib.q_b200_fill_tokens(Q.ptr(toks), PREFILL, SEED, 9, 0, 32000)
+        for _ in range(max(1, args.steps)):
+            ms.forward(toks, 0)
+        print(json.dumps({"only": "prefill", "calls": max(1, args.steps)}), flush=True)
         return
     if args.only == "attention":
         import qorus_b200 as Q
@@ -474,6 +526,9 @@ def main():
     step_gbs = step_bytes / (ms * 1e-3 / args.steps) / 1e9
 
     sweep = gemv_sweep(Q, torch, peak, host=not args.no_cpu_baseline) if world == 1 else None
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        prefill = prefill_measure(Q, m, torch, float(peaks.get("bf16_tflops", 1590.0)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -508,6 +563,7 @@ def main():
                               "frac": round(step_gbs / (peak * world), 4)},
             "cpu_baseline": cpu,
             "sweep": sweep,
+            "prefill": prefill,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 16,
                     "d2h_bytes_per_step": CFG8B["vocab"] * 4},
             "gpu_launches": int(launches),

@@ -222,6 +222,9 @@ q_error_code q_b200_selftest_exchange_timeout(uint64_t limit_ns, uint32_t* statu
 /* Number of kernels this library launched since load (all entry points). */
 uint64_t q_b200_kernel_launches(void);
 
+/* Number of device allocations (cudaMalloc) this library made since load. */
+uint64_t q_b200_device_allocations(void);
+
 /* Last CUDA error string seen by the library ("" if none). */
 const char* q_b200_last_error(void);
 

@@ -68,7 +68,7 @@ q_error_code q_alloc_kv_cache(q_context* ctx, size_t kv_size) {
     DevState* s = state_of(ctx, true);
     if (!s) return Q_ERR_ALLOC_FAILED;
     void* p = nullptr;
-    if (!cuda_ok(cudaMalloc(&p, a), "cudaMalloc(kv)")) return Q_ERR_ALLOC_FAILED;
+    if (!cuda_ok(dev_malloc(&p, a), "dev_malloc(kv)")) return Q_ERR_ALLOC_FAILED;
     if (!cuda_ok(cudaMemset(p, 0, a), "cudaMemset(kv)")) {
         cudaFree(p);
         return Q_ERR_ALLOC_FAILED;
@@ -91,7 +91,7 @@ q_error_code q_alloc_arena(q_context* ctx, size_t arena_size) {
     void* h = aligned_alloc(Q_ALIGN, a);
     if (!h) return Q_ERR_ALLOC_FAILED;
     void* d = nullptr;
-    if (!cuda_ok(cudaMalloc(&d, a), "cudaMalloc(arena)")) {
+    if (!cuda_ok(dev_malloc(&d, a), "dev_malloc(arena)")) {
         free(h);
         return Q_ERR_ALLOC_FAILED;
     }
@@ -169,5 +169,7 @@ const char* q_strerror(q_error_code err) {
 
 const char* q_b200_last_error(void) { return last_error_cstr(); }
 uint64_t q_b200_kernel_launches(void) { return g_kernel_launches.load(); }
+
+uint64_t q_b200_device_allocations(void) { return g_device_allocs.load(); }
 
 }  // extern "C"

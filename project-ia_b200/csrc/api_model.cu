@@ -274,7 +274,7 @@ q_error_code q_sample_token(const float* logits, uint32_t vocab_size, float temp
         Q_CUDA(cudaDeviceSynchronize());
         if (w.p) cudaFree(w.p);
         w = SampleOpWork{};
-        if (!cuda_ok(cudaMalloc(&w.p, need), "cudaMalloc(sampler)")) return Q_ERR_ALLOC_FAILED;
+        if (!cuda_ok(dev_malloc(&w.p, need), "dev_malloc(sampler)")) return Q_ERR_ALLOC_FAILED;
         w.bytes = need;
     }
     uint8_t* b = (uint8_t*)w.p;

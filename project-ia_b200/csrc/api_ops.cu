@@ -20,7 +20,7 @@ struct DevBuf {
     ~DevBuf() {
         if (p) cudaFree(p);
     }
-    bool alloc(size_t n) { return cuda_ok(cudaMalloc(&p, n ? n : 16), "cudaMalloc(op)"); }
+    bool alloc(size_t n) { return cuda_ok(dev_malloc(&p, n ? n : 16), "dev_malloc(op)"); }
     float* f() { return (float*)p; }
 };
 
@@ -299,7 +299,7 @@ extern "C" q_error_code q_b200_gemm_q4(const void* d_packed, uint32_t M, uint32_
         Q_CUDA(cudaDeviceSynchronize());
         if (w.p) cudaFree(w.p);
         w = GemmWork{};
-        if (!cuda_ok(cudaMalloc(&w.p, need), "cudaMalloc(gemm workspace)")) return Q_ERR_ALLOC_FAILED;
+        if (!cuda_ok(dev_malloc(&w.p, need), "dev_malloc(gemm workspace)")) return Q_ERR_ALLOC_FAILED;
         w.bytes = need;
     }
     uint8_t* base = (uint8_t*)w.p;

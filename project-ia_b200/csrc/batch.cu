@@ -199,7 +199,7 @@ q_error_code batch_init(DevState* s, uint32_t B) {
     b.tok_cap = c.max_seq_len;
     const size_t kv_seq = (size_t)c.n_layers * t.nkv * c.max_seq_len * 2 * s->hd * 4;
     b.kv_bytes_seq = kv_seq;
-    if (!cuda_ok(cudaMalloc(&b.kv, kv_seq * B), "cudaMalloc(batch kv)")) {
+    if (!cuda_ok(dev_malloc(&b.kv, kv_seq * B), "dev_malloc(batch kv)")) {
         free_batch(s);
         return Q_ERR_ALLOC_FAILED;
     }
@@ -210,7 +210,7 @@ q_error_code batch_init(DevState* s, uint32_t B) {
                          bal(4)};
     size_t total = 0;
     for (size_t v : sz) total += v;
-    if (!cuda_ok(cudaMalloc(&b.base, total), "cudaMalloc(batch state)")) {
+    if (!cuda_ok(dev_malloc(&b.base, total), "dev_malloc(batch state)")) {
         free_batch(s);
         return Q_ERR_ALLOC_FAILED;
     }

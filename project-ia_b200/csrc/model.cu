@@ -22,7 +22,7 @@
 namespace qb200 {
 
 static q_error_code dalloc(DevState* s, void** p, size_t bytes) {
-    if (!cuda_ok(cudaMalloc(p, bytes ? bytes : 16), "cudaMalloc(weights)")) return Q_ERR_ALLOC_FAILED;
+    if (!cuda_ok(dev_malloc(p, bytes ? bytes : 16), "dev_malloc(weights)")) return Q_ERR_ALLOC_FAILED;
     s->weight_allocs.push_back(*p);
     return Q_OK;
 }
@@ -79,7 +79,7 @@ q_error_code upload_model(q_context* ctx, DevState* s, const q_llama_model* mode
     const size_t down_aos = (size_t)D * (t.h / 32) * 20;
     const size_t stage_bytes = std::max(qkv_aos, std::max(gu_aos, down_aos));
     uint8_t* stage = nullptr;
-    if (!cuda_ok(cudaMalloc(&stage, stage_bytes), "cudaMalloc(stage)")) return Q_ERR_ALLOC_FAILED;
+    if (!cuda_ok(dev_malloc(&stage, stage_bytes), "dev_malloc(stage)")) return Q_ERR_ALLOC_FAILED;
     q_error_code rc = Q_OK;
     auto h2d = [&](void* dst, const void* src, size_t n) {
         return cuda_ok(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, st), "upload");
@@ -608,7 +608,7 @@ q_error_code capture_trace_graph(q_context* ctx, DevState* s) {
     if (s->g_trace) return Q_OK;
     const uint32_t slots = s->cfg.n_layers * 6 + 4;
     if (!s->trace_buf &&
-        !cuda_ok(cudaMalloc(&s->trace_buf, (size_t)slots * 4 * sizeof(unsigned long long)), "trace buf"))
+        !cuda_ok(dev_malloc(&s->trace_buf, (size_t)slots * 4 * sizeof(unsigned long long)), "trace buf"))
         return Q_ERR_ALLOC_FAILED;
     s->trace_slots = slots;
     s->tr_next = s->trace_buf;
@@ -626,7 +626,7 @@ q_error_code ensure_sample_scratch(DevState* s) {
     if (s->samp_probs) return Q_OK;
     const size_t V = s->cfg.vocab_size;
     void* p = nullptr;
-    if (!cuda_ok(cudaMalloc(&p, V * 5 + 256), "cudaMalloc(sampler scratch)")) return Q_ERR_ALLOC_FAILED;
+    if (!cuda_ok(dev_malloc(&p, V * 5 + 256), "dev_malloc(sampler scratch)")) return Q_ERR_ALLOC_FAILED;
     s->samp_probs = (float*)p;
     s->samp_keep = (uint8_t*)p + (V * 4 + 255) / 256 * 256;
     return Q_OK;

@@ -37,7 +37,7 @@ static q_error_code prefill_workspace(DevState* s, uint32_t S) {
     s->pf_base = nullptr;
     s->pf_tok_host = nullptr;
     s->pf_cap = 0;
-    if (!cuda_ok(cudaMalloc(&s->pf_base, total), "cudaMalloc(prefill workspace)")) return Q_ERR_ALLOC_FAILED;
+    if (!cuda_ok(dev_malloc(&s->pf_base, total), "dev_malloc(prefill workspace)")) return Q_ERR_ALLOC_FAILED;
     if (!cuda_ok(cudaMallocHost(&s->pf_tok_host, (size_t)cap * 4), "pinned prompt ids")) return Q_ERR_ALLOC_FAILED;
     uint8_t* p = s->pf_base;
     s->pf_tok = (uint32_t*)p;

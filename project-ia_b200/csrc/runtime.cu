@@ -10,6 +10,7 @@
 namespace qb200 {
 
 std::atomic<uint64_t> g_kernel_launches{0};
+std::atomic<uint64_t> g_device_allocs{0};
 static std::mutex g_err_mu;
 static std::string g_last_error;
 
@@ -287,7 +288,7 @@ void* op_gemv_scratch(size_t bytes) {
         }
         b = {nullptr, 0};
         void* q = nullptr;
-        if (!cuda_ok(cudaMalloc(&q, bytes), "cudaMalloc(gemv scratch)")) return nullptr;
+        if (!cuda_ok(dev_malloc(&q, bytes), "dev_malloc(gemv scratch)")) return nullptr;
         if (!cuda_ok(cudaMemset(q, 0, bytes), "memset(gemv scratch)")) return nullptr;
         b = {q, bytes};
         register_zero_area(q, ChainPlan::kTicketWords * 4);

@@ -30,6 +30,17 @@ void set_last_error(const char* where, cudaError_t e);
 bool cuda_ok(cudaError_t e, const char* where);
 const char* last_error_cstr();
 extern std::atomic<uint64_t> g_kernel_launches;
+extern std::atomic<uint64_t> g_device_allocs;
+// cudaMalloc, counted (q_b200_device_allocations): every device allocation of
+// the library goes through here.
+inline cudaError_t dev_malloc(void** p, size_t bytes) {
+    g_device_allocs.fetch_add(1, std::memory_order_relaxed);
+    return cudaMalloc(p, bytes);
+}
+template <typename T>
+inline cudaError_t dev_malloc(T** p, size_t bytes) {
+    return dev_malloc(reinterpret_cast<void**>(p), bytes);
+}
 int device_sms();
 cudaStream_t op_stream();  // stream for the kernel-level entry points (per device)
 // cudaFuncAttributeMaxDynamicSharedMemorySize = bytes for `kernel` on the

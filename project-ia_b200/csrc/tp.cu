@@ -197,7 +197,7 @@ q_error_code q_b200_tp_ipc_handle(q_context* ctx, void* out, size_t bytes) {
         const uint32_t vpad = ((hd->vocab_size + s->tp_world - 1) / s->tp_world + 3) / 4 * 4;
         s->peer_slice = (std::max(hd->dim, vpad) + 3) / 4 * 4;
         const size_t nb = tp_buffer_bytes(s->tp_world, s->peer_slice);
-        Q_CUDA(cudaMalloc(&s->peer_buf, nb));
+        Q_CUDA(dev_malloc(&s->peer_buf, nb));
         Q_CUDA(cudaMemset(s->peer_buf, 0, nb));
         Q_CUDA(cudaDeviceSynchronize());
     }

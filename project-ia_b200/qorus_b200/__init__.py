@@ -151,6 +151,7 @@ _SIGS = {
     "q_b200_device_status": (_u32, []),
     "q_b200_selftest_exchange_timeout": (_i, [_u64, _vp]),
     "q_b200_kernel_launches": (_u64, []),
+    "q_b200_device_allocations": (_u64, []),
     "q_b200_last_error": (C.c_char_p, []),
 }
 EXPORTS = tuple(_SIGS)

@@ -63,7 +63,13 @@ def run_batch_vs_oracle(path, cfg, B, lens, steps, seed):
         got = np.zeros(kv_elems, np.float32)
         Q.check(Q.lib.q_b200_batch_kv_read(C.byref(dev.ctx), b, 0, Q.ptr(got), got.nbytes), "kv_read")
         p0 = lens[b]
-        close(got.reshape(shp)[:, :, p0:p0 + steps], kvs[b].reshape(shp)[:, :, p0:p0 + steps])
+        d = got.reshape(shp)[:, :, p0:p0 + steps]
+        r = kvs[b].reshape(shp)[:, :, p0:p0 + steps]
+        close(d[0], r[0])
+        for layer in range(1, cfg.n_layers):
+            rl = np.asarray(r[layer], np.float64)
+            err = np.abs(np.asarray(d[layer], np.float64) - rl)
+            assert err.max() <= max(1.5e-4, 1e-4 * float(np.abs(rl).max())), (b, layer, float(err.max()))
     dev.close()
     orc.close()
 

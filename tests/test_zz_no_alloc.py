@@ -50,6 +50,44 @@ def test_noalloc_matches_gemv_q4_twice(torch, M, K):
         assert (err <= np.maximum(1.5e-4, 1e-4 * np.abs(ref))).all(), f"worst {err.max():.3e}"
 
 
+def test_noalloc_allocates_nothing(torch):
+    """The point of the entry point: its calls make no device allocation.
+    Checked with the library's own count of cudaMalloc calls, in a fresh
+    process so that no earlier test has grown a shared buffer already."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    code = r"""
+import sys
+sys.path.insert(0, %r)
+import numpy as np, torch, qorus_b200 as Q
+M, K = 4096, 4096
+nblk = M * K // 32
+w = np.zeros(nblk * 20, np.uint8)
+Q.lib.q_b200_fill_q4(Q.ptr(w), nblk, 5, 11, 0, 0.001, 0.01, 0)
+dw = torch.from_numpy(w).cuda()
+packed = torch.empty(Q.lib.q_b200_q4_packed_bytes(M, K), dtype=torch.uint8, device="cuda")
+x = torch.randn(K, device="cuda")
+y = torch.empty(M, device="cuda")
+torch.cuda.synchronize()
+Q.check(Q.lib.q_b200_q4_pack(dw.data_ptr(), M, K, packed.data_ptr(), None), "pack")
+torch.cuda.synchronize()
+before = Q.lib.q_b200_device_allocations()
+for _ in range(3):
+    Q.check(Q.lib.q_b200_gemv_q4_noalloc(packed.data_ptr(), M, K, x.data_ptr(), y.data_ptr(), None), "noalloc")
+torch.cuda.synchronize()
+after = Q.lib.q_b200_device_allocations()
+Q.check(Q.lib.q_b200_gemv_q4(packed.data_ptr(), M, K, x.data_ptr(), y.data_ptr(), None), "gemv")
+torch.cuda.synchronize()
+print(before, after, Q.lib.q_b200_device_allocations())
+""" % str(Path(__file__).resolve().parents[1] / "project-ia_b200")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    before, after, with_alloc = map(int, out.stdout.split()[-3:])
+    assert after == before
+    assert with_alloc > after  # the allocating entry point does allocate: the count is live
+
+
 def test_noalloc_rejects_oversized_plan(torch):
     # 262144 x 32: 16384 slabs of one block each, whose partial sums
     # (about 3 MiB) exceed the fixed scratch
