@@ -182,7 +182,7 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
     const size_t budget = 220 * 1024;
     const size_t fixed = gemv_smem_bytes(max_nb, 0, 0, red_slabs);
     if (fixed >= budget) return false;
-    const uint32_t sizes[] = {256, 192, 128, 64};
+    const uint32_t sizes[] = {256, 192, 128, 64, 32, 16};  // the small ones for K up to ~28K
     for (uint32_t sb : sizes) {
         const uint32_t ns = (uint32_t)std::min<size_t>(kMaxStages,
                                                        (budget - fixed) / ((size_t)sb * GEMV_BLOCK_BYTES));
