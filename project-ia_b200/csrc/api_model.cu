@@ -279,7 +279,7 @@ q_error_code q_sample_token(const float* logits, uint32_t vocab_size, float temp
     }
     uint8_t* b = (uint8_t*)w.p;
     SampleParams prm{temperature, top_k, top_p, 0u};
-    // upstream's SIMD path needs V >= 8 and a 32-byte aligned buffer; else its scalar fallback
+    // upstream's vector temperature loop needs V >= 8 and 32-byte aligned logits
     prm.scalar_path = (vocab_size < 8 || ((uintptr_t)logits & 31)) ? 1u : 0u;
     cudaStream_t st = op_stream();
     Q_CUDA(cudaMemcpyAsync(b, logits, V * 4, cudaMemcpyHostToDevice, st));

@@ -261,7 +261,10 @@ bool plan_single(uint32_t M, uint32_t K, GemvPlan& p, ChainPlan& cp) {
 cudaError_t launch_single(const ChainPlan& cp, const GemvPlan& p, const GemvArgs& a, void* scratch,
                           cudaStream_t s) {
     const GemvPlan* m[1] = {&p};
-    return launch_chain(cp, m, &a, scratch, nullptr, nullptr, s, false);
+    // programmatic dependent launch: back-to-back GEMVs on one stream stream
+    // the next one's weights during this one's tail (the kernel waits for the
+    // previous grid before it reads its input or touches its scratch)
+    return launch_chain(cp, m, &a, scratch, nullptr, nullptr, s, true);
 }
 
 cudaError_t pack_q4(const uint8_t* d_aos, const GemvPlan& p, uint32_t interleave_half,

@@ -5,8 +5,12 @@
 //   compute_softmax_with_temp (main.c:311-424): logits * (1 / T) on the
 //     8-wide vector body, logits / T on the tail, then q_softmax_f32_avx2
 //     (softmax.c: the clamped polynomial exp below 8 floor(V/8), expf on the
-//     tail, out = e * (1 / sum)); a caller buffer that is not 32-byte aligned
-//     takes upstream's scalar fallback (division everywhere, expf);
+//     tail, out = e * (1 / sum)); logits that are not 32-byte aligned are
+//     divided by T everywhere, as upstream's unaligned temperature loop does
+//     (its softmax then still runs on its own aligned arena buffer).  With a
+//     NULL context upstream's buffer comes from malloc and its alignment picks
+//     between the two softmax forms at random; this follows the arena case,
+//     the one upstream's q_generate takes;
 //   apply_top_k (main.c:430-519): the k most probable tokens, renormalised by
 //     division by their sum (disabled when k == 0 or k >= V);
 //   apply_top_p (main.c:608-716): after sorting by probability, the shortest
@@ -35,7 +39,7 @@ struct SampleParams {  // device-resident, read by the kernel on every launch
     float temperature;  // < 1e-6: greedy (the kernel leaves the argmax key alone)
     uint32_t top_k;
     float top_p;
-    uint32_t scalar_path;  // upstream's unaligned-buffer fallback (divide, expf)
+    uint32_t scalar_path;  // unaligned logits: divide by T everywhere (upstream's scalar loop)
 };
 
 struct SampleArgs {
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS, 1) sample_kernel(const SampleA
     float sum = 0.0f;
     for (uint32_t i = tid; i < V; i += SAMPLE_THREADS) {
         const float x = __fsub_rn(p[i], mx);
-        const float e = (!prm.scalar_path && i < nv) ? exp_poly(x) : expf(x);
+        const float e = i < nv ? exp_poly(x) : expf(x);
         p[i] = e;
         sum += e;
     }
