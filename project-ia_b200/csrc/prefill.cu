@@ -120,6 +120,16 @@ static cudaError_t launch_pf_gemm(DevState* s, uint32_t S, uint32_t M, uint32_t 
     return cudaGetLastError();
 }
 
+static const void* pf_attn_tc_kernel_g(uint32_t G) {
+    switch (G) {
+        case 1: return (const void*)attn_prefill_tc_kernel<128, 1>;
+        case 2: return (const void*)attn_prefill_tc_kernel<128, 2>;
+        case 4: return (const void*)attn_prefill_tc_kernel<128, 4>;
+        case 8: return (const void*)attn_prefill_tc_kernel<128, 8>;
+        default: return nullptr;
+    }
+}
+
 template <int HD>
 static const void* pf_attn_kernel_g(uint32_t G) {
     switch (G) {
@@ -135,10 +145,12 @@ static cudaError_t launch_pf_attention(DevState* s, float* kv, uint32_t layer, u
                                        cudaStream_t st) {
     const q_llama_config& c = s->cfg;
     const uint32_t G = c.n_heads / c.n_kv_heads, hd = s->hd;
-    const void* kern = hd == 32 ? pf_attn_kernel_g<32>(G) : hd == 64 ? pf_attn_kernel_g<64>(G)
-                                                          : hd == 128 ? pf_attn_kernel_g<128>(G) : nullptr;
+    // head_dim 128 (the Llama-3 shapes): tensor cores; smaller heads: CUDA cores
+    const bool tc = hd == 128;
+    const void* kern = tc ? pf_attn_tc_kernel_g(G)
+                          : hd == 32 ? pf_attn_kernel_g<32>(G) : hd == 64 ? pf_attn_kernel_g<64>(G) : nullptr;
     if (!kern) return cudaErrorInvalidValue;
-    const size_t smem = pf_attn_smem(hd);
+    const size_t smem = tc ? pf_attn_tc_smem(hd) : pf_attn_smem(hd);
     cudaError_t e = ensure_smem_attr(kern, (int)smem);
     if (e != cudaSuccess) return e;
     PfAttnArgs a{};
@@ -151,11 +163,11 @@ static cudaError_t launch_pf_attention(DevState* s, float* kv, uint32_t layer, u
     a.n_kv = s->tp.nkv;
     a.max_seq = c.max_seq_len;
     a.scale = 1.0f / sqrtf((float)hd);  // upstream model.c:1315
-    const uint32_t rq = PF_ATT_Q / G;
+    const uint32_t rq = (tc ? PT_Q : PF_ATT_Q) / G;
     dim3 grid((S + rq - 1) / rq, s->tp.nkv);
     void* params[1] = {&a};
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
-    return cudaLaunchKernel(kern, grid, dim3(PF_ATT_THREADS), params, smem, st);
+    return cudaLaunchKernel(kern, grid, dim3(tc ? PT_THREADS : PF_ATT_THREADS), params, smem, st);
 }
 
 q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t S, uint32_t pos, bool sample) {

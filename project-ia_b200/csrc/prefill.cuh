@@ -768,4 +768,263 @@ __global__ void __launch_bounds__(PF_ATT_THREADS) attn_prefill_kernel(const PfAt
     }
 }
 
+// ---- causal attention of a prompt on the tensor cores ----------------------------------
+// Same mathematics as attn_prefill_kernel (two passes: row maxima, then
+// upstream's softmax and P.V), with the two products on mma.sync m16n8k16
+// (f16 in, f32 accumulate), every operand as fp16 hi + lo halves after a
+// power-of-two scale (per CTA for q, per 64-key chunk for K and for V, all
+// multiplied back exactly) and three MMAs per product (hi*hi, hi*lo, lo*hi).
+// Each chunk's P.V is summed in its own accumulators (12 MMAs) and added to
+// the output in fp32, so the tensor core's truncating accumulation never
+// runs long.  CTA = one KV head x 64 query vectors (its G query heads x 64/G
+// rows); 4 warps, warp w owns vectors 16w..16w+15 (one m16 tile).
+static constexpr uint32_t PT_Q = 64, PT_KC = 64, PT_THREADS = 128;
+static constexpr uint32_t PT_LD = 136;  // padded row of the fp16 tiles (halves): conflict-free ldmatrix
+
+__host__ __device__ inline size_t pf_attn_tc_smem(uint32_t hd) {
+    // qh, ql [Q][LD] | kh, kl [KC][LD] | vh, vl [KC][LD] (fp16) | scales
+    (void)hd;
+    return ((size_t)PT_Q * PT_LD * 2 + (size_t)PT_KC * PT_LD * 4) * 2 + 64;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Block-wide max of |x| over the CTA (128 threads) -> the power-of-two
+// exponent that maps it into [2^14, 2^15).
+__device__ __forceinline__ int pt_block_exponent(float m, float* red) {
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    const float t = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    return pf_exponent(t);
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(PT_THREADS) attn_prefill_tc_kernel(const PfAttnArgs a) {
+    static_assert(HD == 128, "tensor-core prompt attention: head_dim 128");
+    static_assert(PT_Q % G == 0, "query vectors per CTA");
+    constexpr uint32_t RQ = PT_Q / G;
+    extern __shared__ __align__(16) uint8_t ptsm[];
+    __half* qh = reinterpret_cast<__half*>(ptsm);
+    __half* ql = qh + PT_Q * PT_LD;
+    __half* kh = ql + PT_Q * PT_LD;
+    __half* kl = kh + PT_KC * PT_LD;
+    __half* vh = kl + PT_KC * PT_LD;
+    __half* vl = vh + PT_KC * PT_LD;
+    float* red = reinterpret_cast<float*>(vl + PT_KC * PT_LD);  // [4]
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t g = lane >> 2, t = lane & 3;
+    const uint32_t h = blockIdx.y, r0 = blockIdx.x * RQ;
+    const uint32_t D = a.n_heads * HD;
+    const float* head = a.kv + (size_t)h * a.max_seq * 2 * HD;
+    const uint32_t N = a.pos + a.S, nv = N / 8 * 8;
+    const uint32_t last_row = min(a.S, r0 + RQ) - 1;
+    const uint32_t n_keys = a.pos + last_row + 1;
+
+    // ---- q: 64 vectors x 128, scaled, as hi / lo halves ----
+    float qmax = 0.0f;
+    for (uint32_t i = tid; i < PT_Q * (HD / 4); i += PT_THREADS) {
+        const uint32_t v = i / (HD / 4), c = i % (HD / 4), row = r0 + v / G;
+        if (row < a.S) {
+            const float4 x = __ldg(reinterpret_cast<const float4*>(a.q + (size_t)row * D + (h * G + v % G) * HD) + c);
+            qmax = fmaxf(qmax, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+        }
+    }
+    const int eq = pt_block_exponent(qmax, red);
+    const float qmul = ldexpf(1.0f, eq);
+    for (uint32_t i = tid; i < PT_Q * (HD / 4); i += PT_THREADS) {
+        const uint32_t v = i / (HD / 4), c = i % (HD / 4), row = r0 + v / G;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < a.S) x = __ldg(reinterpret_cast<const float4*>(a.q + (size_t)row * D + (h * G + v % G) * HD) + c);
+        __half h0, l0, h1, l1, h2, l2, h3, l3;
+        pf_split(x.x * qmul, h0, l0);
+        pf_split(x.y * qmul, h1, l1);
+        pf_split(x.z * qmul, h2, l2);
+        pf_split(x.w * qmul, h3, l3);
+        *reinterpret_cast<uint2*>(qh + v * PT_LD + 4 * c) = make_uint2(h2_bits(__halves2half2(h0, h1)), h2_bits(__halves2half2(h2, h3)));
+        *reinterpret_cast<uint2*>(ql + v * PT_LD + 4 * c) = make_uint2(h2_bits(__halves2half2(l0, l1)), h2_bits(__halves2half2(l2, l3)));
+    }
+    // one K or V chunk (keys k0 .. k0+63, rows past n_keys zero) -> hi / lo
+    // halves scaled by the chunk's power of two; returns 2^-e
+    auto load_chunk = [&](uint32_t k0, uint32_t off, __half* dh, __half* dl) -> float {
+        float m = 0.0f;
+        for (uint32_t i = tid; i < PT_KC * (HD / 4); i += PT_THREADS) {
+            const uint32_t j = i / (HD / 4), c = i % (HD / 4);
+            if (k0 + j < n_keys) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(head + (size_t)(k0 + j) * 2 * HD + off) + c);
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            }
+        }
+        const int e = pt_block_exponent(m, red);
+        const float mul = ldexpf(1.0f, e);
+        for (uint32_t i = tid; i < PT_KC * (HD / 4); i += PT_THREADS) {
+            const uint32_t j = i / (HD / 4), c = i % (HD / 4);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + j < n_keys) x = __ldg(reinterpret_cast<const float4*>(head + (size_t)(k0 + j) * 2 * HD + off) + c);
+            __half h0, l0, h1, l1, h2, l2, h3, l3;
+            pf_split(x.x * mul, h0, l0);
+            pf_split(x.y * mul, h1, l1);
+            pf_split(x.z * mul, h2, l2);
+            pf_split(x.w * mul, h3, l3);
+            *reinterpret_cast<uint2*>(dh + j * PT_LD + 4 * c) = make_uint2(h2_bits(__halves2half2(h0, h1)), h2_bits(__halves2half2(h2, h3)));
+            *reinterpret_cast<uint2*>(dl + j * PT_LD + 4 * c) = make_uint2(h2_bits(__halves2half2(l0, l1)), h2_bits(__halves2half2(l2, l3)));
+        }
+        return ldexpf(1.0f, -e);
+    };
+    // S[8 key tiles][4] of this warp's 16 vectors against the chunk in kh/kl
+    const uint32_t qa_h = smem_u32(qh) + ((16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1)) * PT_LD + 8 * (lane >> 4)) * 2;
+    const uint32_t qa_l = qa_h + (uint32_t)((ql - qh) * 2);
+    // B (keys x dims) for ldmatrix.x4: matrices (keys 0-7, dims 0-7 | 8-15) of tile n, and of tile n+1
+    const uint32_t kb_h = smem_u32(kh) + (((lane & 7) + 8 * (lane >> 4)) * PT_LD + 8 * ((lane >> 3) & 1)) * 2;
+    const uint32_t kb_l = kb_h + (uint32_t)((kl - kh) * 2);
+    auto scores = [&](float (&S)[8][4]) {
+#pragma unroll
+        for (int n = 0; n < 8; ++n) S[n][0] = S[n][1] = S[n][2] = S[n][3] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+            uint32_t ah[4], al[4];
+            ldsm_x4(qa_h + ks * 32, ah[0], ah[1], ah[2], ah[3]);
+            ldsm_x4(qa_l + ks * 32, al[0], al[1], al[2], al[3]);
+#pragma unroll
+            for (int n = 0; n < 8; n += 2) {
+                uint32_t bh0, bh1, bh2, bh3, bl0, bl1, bl2, bl3;
+                ldsm_x4(kb_h + (n * 8 * PT_LD + ks * 16) * 2, bh0, bh1, bh2, bh3);
+                ldsm_x4(kb_l + (n * 8 * PT_LD + ks * 16) * 2, bl0, bl1, bl2, bl3);
+                mma16816(S[n], ah, bh0, bh1);
+                mma16816(S[n], ah, bl0, bl1);
+                mma16816(S[n], al, bh0, bh1);
+                mma16816(S[n + 1], ah, bh2, bh3);
+                mma16816(S[n + 1], ah, bl2, bl3);
+                mma16816(S[n + 1], al, bh2, bh3);
+            }
+        }
+    };
+    // this lane's rows: vectors 16 warp + g (e < 2) and + 8 (e >= 2)
+    uint32_t last[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) last[hh] = a.pos + r0 + (16 * warp + g + 8 * hh) / G;
+    const float unq = ldexpf(1.0f, -eq);
+
+    // ---- pass 1: row maxima ----
+    float mx[2] = {-INFINITY, -INFINITY};
+    for (uint32_t k0 = 0; k0 < n_keys; k0 += PT_KC) {
+        __syncthreads();
+        const float unk = load_chunk(k0, 0, kh, kl);
+        __syncthreads();
+        float S[8][4];
+        scores(S);
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t key = k0 + 8 * n + 2 * t + (e & 1);
+                const float sv = __fmul_rn(S[n][e] * unq * unk, a.scale);
+                if (key <= last[e >> 1]) mx[e >> 1] = fmaxf(mx[e >> 1], sv);
+            }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 1));
+        mx[hh] = fmaxf(mx[hh], __shfl_xor_sync(0xffffffffu, mx[hh], 2));
+    }
+
+    // ---- pass 2: exponentials, sums, P.V ----
+    float O[16][4];
+#pragma unroll
+    for (int d = 0; d < 16; ++d) O[d][0] = O[d][1] = O[d][2] = O[d][3] = 0.0f;
+    float l[2] = {0.0f, 0.0f};
+    // V (keys x dims) with .trans: matrices (keys 0-7 | 8-15) x (dims of tile d | d+1)
+    const uint32_t vb_h = smem_u32(vh) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * PT_LD + 8 * (lane >> 4)) * 2;
+    const uint32_t vb_l = vb_h + (uint32_t)((vl - vh) * 2);
+    for (uint32_t k0 = 0; k0 < n_keys; k0 += PT_KC) {
+        __syncthreads();
+        const float unk = load_chunk(k0, 0, kh, kl);
+        const float unv = load_chunk(k0, HD, vh, vl);
+        __syncthreads();
+        float S[8][4];
+        scores(S);
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t key = k0 + 8 * n + 2 * t + (e & 1);
+                float p = 0.0f;
+                if (key <= last[e >> 1]) {
+                    const float x = __fsub_rn(__fmul_rn(S[n][e] * unq * unk, a.scale), mx[e >> 1]);
+                    p = key < nv ? exp_poly(x) : expf(x);
+                }
+                l[e >> 1] = __fadd_rn(l[e >> 1], p);
+                S[n][e] = p;
+            }
+        // P (C fragments) -> A fragments, hi and lo halves; this chunk's P.V
+        float Oc[16][4];
+#pragma unroll
+        for (int d = 0; d < 16; ++d) Oc[d][0] = Oc[d][1] = Oc[d][2] = Oc[d][3] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < PT_KC / 16; ++ks) {
+            uint32_t ph[4], pl[4];
+            const float* s0 = S[2 * ks];
+            const float* s1 = S[2 * ks + 1];
+            const float src[4][2] = {{s0[0], s0[1]}, {s0[2], s0[3]}, {s1[0], s1[1]}, {s1[2], s1[3]}};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const __half2 hv = __floats2half2_rn(src[r][0], src[r][1]);
+                const float2 hf = __half22float2(hv);
+                ph[r] = h2_bits(hv);
+                pl[r] = h2_bits(__floats2half2_rn(src[r][0] - hf.x, src[r][1] - hf.y));
+            }
+#pragma unroll
+            for (int d = 0; d < 16; d += 2) {
+                uint32_t bh0, bh1, bh2, bh3, bl0, bl1, bl2, bl3;
+                ldsm_x4_t(vb_h + (ks * 16 * PT_LD + d * 8) * 2, bh0, bh1, bh2, bh3);
+                ldsm_x4_t(vb_l + (ks * 16 * PT_LD + d * 8) * 2, bl0, bl1, bl2, bl3);
+                mma16816(Oc[d], ph, bh0, bh1);
+                mma16816(Oc[d], ph, bl0, bl1);
+                mma16816(Oc[d], pl, bh0, bh1);
+                mma16816(Oc[d + 1], ph, bh2, bh3);
+                mma16816(Oc[d + 1], ph, bl2, bl3);
+                mma16816(Oc[d + 1], pl, bh2, bh3);
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < 16; ++d)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) O[d][e] = __fadd_rn(O[d][e], Oc[d][e] * unv);
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        l[hh] += __shfl_xor_sync(0xffffffffu, l[hh], 1);
+        l[hh] += __shfl_xor_sync(0xffffffffu, l[hh], 2);
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t v = 16 * warp + g + 8 * hh, row = r0 + v / G;
+        if (row >= a.S) continue;
+        const float inv = __fdiv_rn(1.0f, l[hh]);
+        float* o = a.out + (size_t)row * D + (h * G + v % G) * HD;
+#pragma unroll
+        for (int d = 0; d < 16; ++d)
+            *reinterpret_cast<float2*>(o + 8 * d + 2 * t) =
+                make_float2(__fmul_rn(O[d][2 * hh], inv), __fmul_rn(O[d][2 * hh + 1], inv));
+    }
+}
+
 }  // namespace qb200

@@ -155,3 +155,36 @@ def test_llama8b_shapes_prompt_2048_vs_oracle(llama8b_2layer):
     assert np.abs(a - b).max() <= LOGIT_TOL and int(np.argmax(a)) == int(np.argmax(b))
     dev.close()
     orc.close()
+
+
+@pytest.fixture(scope="module")
+def hd128_path(tmp_path_factory):
+    # a small model with Llama-3's head size (128) and grouping (4 query heads per KV head)
+    cfg = Q.config(259, 512, 1024, 2, 4, 1, 640)
+    path = tmp_path_factory.mktemp("hd128") / "hd128.qorus"
+    Q.write_model(str(path), cfg, seed=5)
+    return str(path), cfg
+
+
+def test_head128_prompt_chunks_vs_oracle(hd128_path):
+    """The tensor-core prompt attention (head_dim 128): a 300-row prompt, then
+    a 77-row chunk at pos 300 (keys from the earlier call in the cache, the
+    causal mask inside the chunk, a row length that is not a multiple of 8 so
+    the tail takes expf), then a decode step over what the prompts wrote."""
+    path, cfg = hd128_path
+    dev, orc = Q.Model(path), O.OracleModel(path)
+    toks = np.zeros(377, np.uint32)
+    Q.lib.q_b200_fill_tokens(Q.ptr(toks), toks.size, 8, 1, 0, 259)
+    for lo, hi in ((0, 300), (300, 377)):
+        a = dev.forward(toks[lo:hi], lo).copy()
+        b = orc.forward(toks[lo:hi], lo)
+        assert np.abs(a - b).max() <= LOGIT_TOL and int(np.argmax(a)) == int(np.argmax(b))
+        kv = np.zeros(orc.kv.size, np.float32)
+        dev.kv_read(kv)
+        kv_rows_close(kv, orc.kv, cfg, 0, hi)
+    tok = int(np.argmax(b))
+    a = dev.forward(np.array([tok], np.uint32), 377).copy()
+    b = orc.forward(np.array([tok], np.uint32), 377)
+    assert np.abs(a - b).max() <= LOGIT_TOL and int(np.argmax(a)) == int(np.argmax(b))
+    dev.close()
+    orc.close()

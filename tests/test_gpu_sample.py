@@ -152,16 +152,17 @@ def test_sample_token_matches_upstream(temp, k, p, V):
         # sequential fp32 running sum over 10^5 terms, so the edge margin is wider.
         logits[:] = rng.uniform(-0.9, 0.9, V).astype(np.float32) * temp
         delta = 2e-4
-    ours = in_fresh_thread(lambda: draws(Q.lib, logits, temp, k, p, 40))
+    n = 40 if V < 1000 else 12  # upstream sorts the whole vocabulary per draw for top-p
+    ours = in_fresh_thread(lambda: draws(Q.lib, logits, temp, k, p, n))
     assert len(set(ours)) > 1 or k == 1  # it does draw, not always the argmax
     ids, cdf = kept_cdf(np.asarray(logits), temp, k, p)
-    rs = xorshift_draws(40)
+    rs = xorshift_draws(n)
     for a, r in zip(ours, rs):
         assert consistent(a, r, ids, cdf, delta), (a, r)
     if O.ref is None:
         return
-    ref1 = in_fresh_thread(lambda: draws(O.ref, logits, temp, k, p, 40))
-    ref2 = in_fresh_thread(lambda: draws(O.ref, logits, temp, k, p, 40))
+    ref1 = in_fresh_thread(lambda: draws(O.ref, logits, temp, k, p, n))
+    ref2 = in_fresh_thread(lambda: draws(O.ref, logits, temp, k, p, n))
     if ref1 != ref2:
         return  # upstream's binary is not repeatable on these inputs (see the module note)
     for a, b, r in zip(ours, ref1, rs):
