@@ -113,15 +113,34 @@ q_error_code llama_forward(q_llama_model* Q_RESTRICT model, q_context* Q_RESTRIC
 /* ---- generation (upstream src/main.c) ---------------------------------- */
 
 /* upstream include/qorus.h:292 — greedy when temperature < 1e-6 (first
- * index of the maximum); other settings return Q_ERR_INVALID_ARG in this
- * build (sampling is outside the B200 hot path). */
+ * index of the maximum); otherwise temperature, top-k, top-p and one draw of
+ * the per-thread xorshift64* stream, computed on the device. */
 q_error_code q_sample_token(const float* Q_RESTRICT logits, uint32_t vocab_size,
                             float temperature, uint32_t top_k, float top_p,
                             uint32_t* Q_RESTRICT token_id_out, q_context* Q_RESTRICT ctx);
 
-/* upstream include/qorus.h:318 — prefill then greedy decode; the argmax is
- * taken on the device, so no logits cross PCIe per token. */
+/* upstream include/qorus.h:318 — prefill, then decode with greedy argmax or
+ * the sampler on the device, so no logits cross PCIe per token. */
 q_error_code q_generate(q_generation_state* Q_RESTRICT state);
+
+/* ---- tokenizer (upstream src/tokenizer/bpe.c, host code) --------------- */
+
+/* upstream include/qorus.h:230 — read a 'QTKR' v1 tokenizer file. */
+q_error_code q_tokenizer_load(q_tokenizer* Q_RESTRICT tok, const char* tokenizer_path);
+
+/* upstream include/qorus.h:242 — byte ids, greedy BPE merges in rule order,
+ * optional BOS/EOS; Q_ERR_ARENA_OOM when the result exceeds max_tokens. */
+q_error_code q_tokenizer_encode(q_tokenizer* Q_RESTRICT tok, const char* Q_RESTRICT text,
+                                uint32_t* Q_RESTRICT tokens_out, uint32_t* Q_RESTRICT num_tokens_out,
+                                uint32_t max_tokens, bool add_bos, bool add_eos);
+
+/* upstream include/qorus.h:260 — concatenated token strings, special and
+ * out-of-range ids skipped; Q_ERR_ARENA_OOM (truncated) when it does not fit. */
+q_error_code q_tokenizer_decode(q_tokenizer* Q_RESTRICT tok, const uint32_t* Q_RESTRICT tokens,
+                                uint32_t num_tokens, char* Q_RESTRICT text_out, size_t text_buf_size);
+
+/* upstream include/qorus.h:273 — release everything and zero the struct. */
+void q_tokenizer_free(q_tokenizer* Q_RESTRICT tok);
 
 #ifdef __cplusplus
 }

@@ -10,3 +10,4 @@
 #include "api_model.cu"
 #include "api_ops.cu"
 #include "api_noalloc.cu"
+#include "tokenizer.cu"

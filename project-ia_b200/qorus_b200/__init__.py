@@ -118,6 +118,10 @@ _SIGS = {
     "llama_forward": (_i, [_vp, _vp, _vp, _u32, _u32, _vp]),
     "q_sample_token": (_i, [_vp, _u32, _f, _u32, _f, _vp, _vp]),
     "q_generate": (_i, [_vp]),
+    "q_tokenizer_load": (_i, [_vp, C.c_char_p]),
+    "q_tokenizer_encode": (_i, [_vp, C.c_char_p, _vp, _vp, C.c_uint32, C.c_bool, C.c_bool]),
+    "q_tokenizer_decode": (_i, [_vp, _vp, C.c_uint32, _vp, _sz]),
+    "q_tokenizer_free": (None, [_vp]),
     "q_b200_model_file_size": (_sz, [_vp]),
     "q_b200_write_model_file": (_i, [C.c_char_p, _vp, _u64, _i]),
     "q_b200_fill_normal": (None, [_vp, _sz, _u64, _u64, _u64, _f, _f, _i]),
