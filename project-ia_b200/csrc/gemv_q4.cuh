@@ -121,12 +121,63 @@ struct GemvTp {
     uint32_t tp_send, tp_recv, tp_par, tp_expect;
 };
 
+static constexpr uint32_t GEMV_TP_MAX_CTAS = 256;  // flag words per (parity, rank)
+
+// Control words after the flags (u32 index from the control base):
+// ticket[2] | seq[2] | head ticket | key seq | 2 spare | key flag[8] |
+// key[8] (u64, the LM head's argmax key of each rank).
+static constexpr uint32_t TP_CTL_HEAD_TICKET = 4, TP_CTL_KEY_SEQ = 5, TP_CTL_KEY_FLAG = 8, TP_CTL_KEY = 16;
+
+__device__ __forceinline__ uint32_t* tp_flag_base(const GemvTp& t, uint32_t rank) {
+    return reinterpret_cast<uint32_t*>(t.tp_base[rank] + t.tp_off + (size_t)2 * t.tp_world * t.tp_slice * 4);
+}
+__device__ __forceinline__ uint32_t* tp_ctl(const GemvTp& t, uint32_t rank) {
+    return tp_flag_base(t, rank) + (size_t)2 * t.tp_world * GEMV_TP_MAX_CTAS;
+}
+
+// Receive side of an exchange of parity t.tp_par, run by the T threads of
+// named barrier 1 in every CTA of the grid: wait (bounded) until the
+// t.tp_expect flags (W ranks x the sending grid) carry this exchange's
+// sequence number — this rank's count of completed receives of the parity,
+// plus one — then the last CTA past the wait (local ticket) advances the
+// count.  Nothing is cleared, so a flag that lands late (after a timed-out
+// wait) is below the next exchange's number and cannot release it.
+// Returns this rank's receive slots of the parity, [W][tp_slice] fp32.
+__device__ __forceinline__ const float* tp_recv_wait(const GemvTp& t, uint32_t tid, uint32_t T) {
+    const uint32_t* flag = tp_flag_base(t, t.tp_rank) + (size_t)t.tp_par * t.tp_world * GEMV_TP_MAX_CTAS;
+    uint32_t* ctl = tp_ctl(t, t.tp_rank);
+    uint32_t* ticket = ctl + t.tp_par;
+    uint32_t* seqw = ctl + 2 + t.tp_par;
+    const uint32_t want = __ldcg(seqw) + 1u;
+    const uint32_t per = t.tp_expect / t.tp_world;
+    const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
+    for (uint32_t i = tid; i < t.tp_expect; i += T) {
+        const uint32_t* f = flag + (size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per;
+        while ((int32_t)(ld_acquire_sys(f) - want) < 0) {
+            if (gtimer() - t0 > lim) {
+                qdev_fail(QDEV_PEER_TIMEOUT);
+                break;
+            }
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(T));
+    if (tid == 0) {
+        uint32_t old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
+        if (old == gridDim.x - 1) {  // every CTA has read `want`
+            *ticket = 0u;
+            __stcg(seqw, want);
+        }
+    }
+    return reinterpret_cast<const float*>(t.tp_base[t.tp_rank] + t.tp_off) +
+           (size_t)t.tp_par * t.tp_world * t.tp_slice;
+}
+
 // A chain of up to GEMV_MAX_PHASES GEMVs run by one persistent grid: phase
 // p + 1 reads what phase p wrote, so consumers pass a grid barrier between
 // phases, while the producer warps stream the next matrices' weights
 // straight through it (weights never depend on activations).
 static constexpr int GEMV_MAX_PHASES = 4;
-static constexpr uint32_t GEMV_TP_MAX_CTAS = 256;  // flag words per (parity, rank)
 struct GemvChain {
     GemvArgs ph[GEMV_MAX_PHASES];
     uint32_t n_phases;
@@ -137,6 +188,7 @@ struct GemvChain {
     uint32_t* bar;              // n_phases counters, zero between launches (n_phases > 1)
     unsigned long long* trace;  // step-trace slot (null: off)
     GemvTp tp;                  // single-phase launches of q4_slab_kernel<true> only
+    L2Range l2pf[2];            // weights of later kernels, pulled into L2 while this one runs
 };
 
 // Shared memory: ring | bfrag[max_nb][144] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
@@ -297,44 +349,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     float r_norm = 1.0f;
     const float4* rx4 = nullptr;  // tensor-parallel receive slots of this exchange, [W][tp_slice]
     const GemvTp& tpa = c.tp;
-    if (TP && tpa.tp_recv) {
-        uint8_t* mine = tpa.tp_base[tpa.tp_rank] + tpa.tp_off;
-        uint32_t* flag = reinterpret_cast<uint32_t*>(mine + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4) +
-                         (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS;
-        rx4 = reinterpret_cast<const float4*>(mine + (size_t)tpa.tp_par * tpa.tp_world * tpa.tp_slice * 4);
-        // flags of sending CTAs 0..tp_expect/W-1 of every rank.  Flags carry
-        // the exchange's sequence number (this rank's count of completed
-        // receives of this parity, plus one): every CTA of this grid waits
-        // until each flag has reached it, then the last CTA past the wait
-        // (local ticket) advances the count.  Nothing is cleared, so a flag
-        // that lands late (after a timed-out wait) is below the next
-        // exchange's number and cannot release it.
-        uint32_t* ctl = flag - (size_t)tpa.tp_par * tpa.tp_world * GEMV_TP_MAX_CTAS +
-                        (size_t)2 * tpa.tp_world * GEMV_TP_MAX_CTAS;  // ticket[2] | seq[2]
-        uint32_t* ticket = ctl + tpa.tp_par;
-        uint32_t* seqw = ctl + 2 + tpa.tp_par;
-        const uint32_t want = __ldcg(seqw) + 1u;
-        const uint32_t per = tpa.tp_expect / tpa.tp_world;
-        const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
-        for (uint32_t i = tid; i < tpa.tp_expect; i += T) {
-            const uint32_t* f = flag + (size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per;
-            while ((int32_t)(ld_acquire_sys(f) - want) < 0) {
-                if (gtimer() - t0 > lim) {
-                    qdev_fail(QDEV_PEER_TIMEOUT);
-                    break;
-                }
-            }
-        }
-        asm volatile("bar.sync 1, %0;" ::"r"(T));
-        if (tid == 0) {
-            uint32_t old;
-            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
-            if (old == gridDim.x - 1) {  // every CTA has read `want`
-                *ticket = 0u;
-                __stcg(seqw, want);
-            }
-        }
-    }
+    if (TP && tpa.tp_recv) rx4 = reinterpret_cast<const float4*>(tp_recv_wait(tpa, tid, T));
     for (uint32_t base = 0; base < n4; base += T * NR) {
         float4 xv[NR];
         if (!TP || !rx4) {
@@ -643,12 +658,10 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         // rank tid
         // (flag value: this exchange's sequence number, from this rank's
         // own receive count of the parity; every rank counts the same)
-        const uint32_t* own = reinterpret_cast<const uint32_t*>(
-            tpa.tp_base[tpa.tp_rank] + tpa.tp_off + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4);
-        const uint32_t seq = __ldcg(own + (size_t)2 * tpa.tp_world * GEMV_TP_MAX_CTAS + 2 + tpa.tp_par) + 1u;
+        const uint32_t seq = __ldcg(tp_ctl(tpa, tpa.tp_rank) + 2 + tpa.tp_par) + 1u;
         __threadfence_system();
-        uint32_t* f = reinterpret_cast<uint32_t*>(tpa.tp_base[tid] + tpa.tp_off + (size_t)2 * tpa.tp_world * tpa.tp_slice * 4);
-        st_release_sys(f + ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * GEMV_TP_MAX_CTAS + cta, seq);
+        st_release_sys(tp_flag_base(tpa, tid) + ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * GEMV_TP_MAX_CTAS + cta,
+                       seq);
     }
 }
 
@@ -697,6 +710,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1)
     if (tid >= T) {
         // ---- producer warp: every phase's block range, back to back ----------
         if (tid == T) {
+            l2_prefetch_share(c.l2pf[0], cta, G);
+            l2_prefetch_share(c.l2pf[1], cta, G);
             const uint64_t pol = l2_evict_first_policy();
             uint32_t s = 0, ph = 0, k = 0;  // ring slot, its parity, stages issued
             bool ok = true;

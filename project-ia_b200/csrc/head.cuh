@@ -34,6 +34,17 @@ struct HeadArgs {
     float* logits;             // [rows]
     unsigned long long* best;  // argmax key (null: none)
     unsigned long long* trace; // step-trace slot (null: off)
+    // Tensor-parallel exchange (peer memory; see GemvTp):
+    //   tp.tp_recv: x is not read; the input is the rank-order sum of the W
+    //   slots of parity tp.tp_par that the last layer's down projection sent,
+    //   and CTA 0 stores that sum (the residual stream) to x_copy;
+    //   tp_key: once every CTA has folded its rows into *best (local ticket),
+    //   the last CTA stores the key to key[rank] of every rank and raises
+    //   key_flag[rank] to the key exchange's sequence number; advance_kernel
+    //   takes the maximum of the W keys.
+    GemvTp tp;
+    float* x_copy;
+    uint32_t tp_key;
 };
 
 // Shared memory: ring[slots][HEAD_STAGE_BYTES] | x[K] fp32.
@@ -112,10 +123,22 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs
     // ---- consumers: normalised x into shared memory ------------------------------------
     pdl_wait();
     if (tid == 0) trace_mark(a.trace, 1);
+    if (a.tp.tp_recv) {
+        const float* rx = tp_recv_wait(a.tp, tid, T);
+        for (uint32_t i = tid; i < K; i += T) {
+            float v = __ldcg(rx + i);  // the W slots in rank order, as the one-shot all-reduce adds them
+            for (uint32_t q = 1; q < a.tp.tp_world; ++q) v = __fadd_rn(v, __ldcg(rx + (size_t)q * a.tp.tp_slice + i));
+            xs[i] = v;
+            if (a.x_copy && blockIdx.x == 0) a.x_copy[i] = v;
+        }
+    } else {
+        for (uint32_t i = tid; i < K; i += T) xs[i] = a.x[i];
+    }
+    // (each thread normalises the elements it stored, so no barrier yet)
     float r = 1.0f;
     if (a.norm_w) {
         float ss = 0.0f;
-        for (uint32_t i = tid; i < K; i += T) ss = __fmaf_rn(a.x[i], a.x[i], ss);
+        for (uint32_t i = tid; i < K; i += T) ss = __fmaf_rn(xs[i], xs[i], ss);
         ss = warp_sum(ss);
         if (lane == 0) part[warp] = ss;
         asm volatile("bar.sync 1, %0;" ::"r"(T));
@@ -126,7 +149,8 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs
         float tm = __fsub_rn(3.0f, __fmul_rn(me, __fmul_rn(r0f, r0f)));
         r = __fmul_rn(__fmul_rn(r0f, tm), 0.5f);
     }
-    for (uint32_t i = tid; i < K; i += T) xs[i] = a.norm_w ? __fmul_rn(__fmul_rn(a.x[i], r), a.norm_w[i]) : a.x[i];
+    if (a.norm_w)
+        for (uint32_t i = tid; i < K; i += T) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), a.norm_w[i]);
     asm volatile("bar.sync 1, %0;" ::"r"(T));
 
     // ---- consumers: stages ----------------------------------------------------------
@@ -190,6 +214,25 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs
         unsigned long long b = 0ull;
         for (int i = 0; i < HEAD_CWARPS; ++i) b = wbest[i] > b ? wbest[i] : b;
         if (b) atomicMax(a.best, b);
+        if (a.tp_key) {
+            uint32_t* ctl = tp_ctl(a.tp, a.tp.tp_rank);
+            uint32_t old;
+            __threadfence();
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                         : "=r"(old)
+                         : "l"(ctl + TP_CTL_HEAD_TICKET)
+                         : "memory");
+            if (old == gridDim.x - 1) {  // every CTA's key is folded in
+                ctl[TP_CTL_HEAD_TICKET] = 0u;
+                const unsigned long long k = atomicAdd(a.best, 0ull);
+                const uint32_t seq = __ldcg(ctl + TP_CTL_KEY_SEQ) + 1u;
+                for (uint32_t q = 0; q < a.tp.tp_world; ++q)
+                    *reinterpret_cast<volatile unsigned long long*>(tp_ctl(a.tp, q) + TP_CTL_KEY + 2 * a.tp.tp_rank) = k;
+                __threadfence_system();
+                for (uint32_t q = 0; q < a.tp.tp_world; ++q)
+                    st_release_sys(tp_ctl(a.tp, q) + TP_CTL_KEY_FLAG + a.tp.tp_rank, seq);
+            }
+        }
         trace_mark(a.trace, 2);
     }
 }
@@ -204,6 +247,8 @@ struct AdvanceArgs {
     uint32_t token_cap;
     uint32_t* last_token;      // most recent argmax
     unsigned long long* trace; // step-trace slot (null: off)
+    uint32_t* key_ctl;         // tensor parallel: this rank's exchange control words (null: *best alone)
+    uint32_t key_world;
 };
 
 __global__ void advance_kernel(const AdvanceArgs a) {
@@ -212,7 +257,24 @@ __global__ void advance_kernel(const AdvanceArgs a) {
     pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     trace_mark(a.trace, 1);
-    const unsigned long long k = *a.best;
+    unsigned long long k = *a.best;
+    if (a.key_ctl) {  // the maximum of every rank's key (the LM head's tp_key exchange)
+        const uint32_t want = __ldcg(a.key_ctl + TP_CTL_KEY_SEQ) + 1u;
+        const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
+        k = 0ull;
+        for (uint32_t q = 0; q < a.key_world; ++q) {
+            while ((int32_t)(ld_acquire_sys(a.key_ctl + TP_CTL_KEY_FLAG + q) - want) < 0) {
+                if (gtimer() - t0 > lim) {
+                    qdev_fail(QDEV_PEER_TIMEOUT);
+                    break;
+                }
+            }
+            const unsigned long long v =
+                *reinterpret_cast<volatile const unsigned long long*>(a.key_ctl + TP_CTL_KEY + 2 * q);
+            k = v > k ? v : k;
+        }
+        __stcg(a.key_ctl + TP_CTL_KEY_SEQ, want);
+    }
     const uint32_t tok = 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
     *a.last_token = tok;
     const uint32_t n = *a.token_count;

@@ -356,8 +356,11 @@ static q_error_code make_kv_map(DevState* s, void* kv) {
     return Q_OK;
 }
 
-static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t st) {
+static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t st, L2Range pf0 = {},
+                                     L2Range pf1 = {}) {
     AttnArgs a{};
+    a.l2pf[0] = pf0;
+    a.l2pf[1] = pf1;
     a.q = s->q;
     a.layer = layer;
     a.trace = take_slot(s);
@@ -449,12 +452,15 @@ static bool tp_fused(const DevState* s) {
     const char* e = getenv("QORUS_B200_TP_FUSED");
     return !(e && e[0] == '0');
 }
-static void tp_fuse(const DevState* s, GemvArgs& g, GemvTp& t, bool send, uint32_t par, uint32_t expect) {
+static void tp_geometry(const DevState* s, GemvTp& t) {
     for (uint32_t r = 0; r < s->tp_world; ++r) t.tp_base[r] = s->peers.base[r];
     t.tp_off = (uint32_t)tp_fused_offset(s->tp_world, s->peer_slice);
     t.tp_slice = s->peer_slice;
     t.tp_world = s->tp_world;
     t.tp_rank = s->tp_rank;
+}
+static void tp_fuse(const DevState* s, GemvArgs& g, GemvTp& t, bool send, uint32_t par, uint32_t expect) {
+    tp_geometry(s, t);
     t.tp_par = par;
     if (send) {
         t.tp_send = 1;
@@ -465,14 +471,26 @@ static void tp_fuse(const DevState* s, GemvArgs& g, GemvTp& t, bool send, uint32
     }
 }
 
-static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
+// head_recv: the LM head follows and takes the last layer's down exchange
+// itself (fused tensor-parallel exchange only).
+static L2Range l2_slice(const uint8_t* w, size_t total, double off_mb, double mb) {
+    const size_t off = std::min(total, (size_t)(off_mb * 1048576.0) / 256 * 256);
+    const size_t n = std::min(total - off, (size_t)(mb * 1048576.0) / 256 * 256);
+    return n ? L2Range{w + off, (uint32_t)n} : L2Range{};
+}
+
+static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st, bool head_recv = false) {
     const q_llama_config& c = s->cfg;
+    double kn[5] = {0, 0, 0, 0, 0};  // EXPERIMENT: att_wo, att_gu, wo_gu, gu_down, down_qkv (MB)
+    if (const char* e = getenv("QB_EXP_L2PF"))
+        sscanf(e, "%lf,%lf,%lf,%lf,%lf", &kn[0], &kn[1], &kn[2], &kn[3], &kn[4]);
     const uint32_t D = c.dim;
     GemvArgs first = qkv_args(s, kv, 0);
     const GemvPlan* fm[1] = {&s->p_qkv};
     cudaError_t e = launch_chain(s->cp_first, fm, &first, s->gemv_scratch, nullptr, take_slot(s), st, false);
     for (uint32_t l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
-        e = enqueue_attention(s, l, st);
+        e = enqueue_attention(s, l, st, l2_slice(s->wo[l], s->p_wo.packed_bytes, 0, kn[0]),
+                              l2_slice(s->gu[l], s->p_gu.packed_bytes, 0, kn[1]));
         if (e != cudaSuccess) break;
         GemvArgs ph[4] = {};
         ph[0].w = s->wo[l];  // attention output -> residual
@@ -496,14 +514,18 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
         ph[2].epi = residual_epi(s);
         const bool more = l + 1 < c.n_layers;
         if (more) ph[3] = qkv_args(s, kv, l + 1);
+        const L2Range pfs[4] = {l2_slice(s->gu[l], s->p_gu.packed_bytes, kn[1], kn[2]),
+                                l2_slice(s->down[l], s->p_down.packed_bytes, 0, kn[3]),
+                                more ? l2_slice(s->qkv[l + 1], s->p_qkv.packed_bytes, 0, kn[4]) : L2Range{},
+                                L2Range{}};
         GemvTp tps[4] = {};
         if (tp_fused(s)) {
             tp_fuse(s, ph[0], tps[0], true, 0, 0);
             tp_fuse(s, ph[1], tps[1], false, 0, s->cp_wo.grid * s->tp_world);
-            if (more) {  // the last layer's down feeds the head through the all-reduce kernel
-                tp_fuse(s, ph[2], tps[2], true, 1, 0);
-                tp_fuse(s, ph[3], tps[3], false, 1, s->cp_down.grid * s->tp_world);
-            }
+            // the last layer's down feeds the LM head's prologue, or (rows
+            // without a head) the all-reduce kernel
+            if (more || head_recv) tp_fuse(s, ph[2], tps[2], true, 1, 0);
+            if (more) tp_fuse(s, ph[3], tps[3], false, 1, s->cp_down.grid * s->tp_world);
         }
         const GemvPlan* mats[4] = {&s->p_wo, &s->p_gu, &s->p_down, &s->p_qkv};
         if (s->chain_phases > 1) {
@@ -514,7 +536,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
             const ChainPlan* one[4] = {&s->cp_wo, &s->cp_gu, &s->cp_down, &s->cp_first};
             for (uint32_t i = 0; i < (more ? 4u : 3u) && e == cudaSuccess; ++i) {
                 e = launch_chain(*one[i], &mats[i], &ph[i], s->gemv_scratch, nullptr, take_slot(s), st, true,
-                                 &tps[i]);
+                                 &tps[i], pfs[i]);
                 // wo and down hold partial residual updates on a tensor-parallel rank
                 if (e == cudaSuccess && (i == 0 || i == 2) && !tps[i].tp_send) e = allreduce_sum(s, s->x, c.dim, st);
             }
@@ -527,8 +549,20 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st) {
 // residual stream), optionally the sampler (which replaces the argmax key
 // with a drawn token when the context's temperature is above 0), then the
 // step advance.
-static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = nullptr, bool sample = false) {
+static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = nullptr, bool sample = false,
+                                bool tp_recv = false) {
     HeadArgs h{};
+    const bool fused = tp_fused(s);
+    if (fused) {  // argmax keys over peer memory; the receive of the last down exchange if asked
+        tp_geometry(s, h.tp);
+        h.tp_key = 1;
+        if (tp_recv) {
+            h.tp.tp_recv = 1;
+            h.tp.tp_par = 1;
+            h.tp.tp_expect = s->cp_down.grid * s->tp_world;
+            h.x_copy = s->x;
+        }
+    }
     h.w = s->out_w;
     h.x = x ? x : s->x;
     h.norm_w = s->out_norm;
@@ -550,7 +584,9 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
     const size_t smem = head_smem_bytes(h.K, h.slots);
     cudaError_t e = launch_ex(lm_head_kernel, dim3(grid), dim3(HEAD_THREADS), smem, st, true, h);
     if (e != cudaSuccess) return e;
-    if (s->tp_world > 1 && s->peers_ready) {  // the argmax key over every rank's vocab rows
+    if (fused) {
+        // advance_kernel reduces the keys
+    } else if (s->tp_world > 1 && s->peers_ready) {  // the argmax key over every rank's vocab rows
         e = tp_allreduce(s, s->best, 1, TP_MAX_U64, st);
         if (e != cudaSuccess) return e;
     } else if (s->tp_world > 1) {
@@ -580,6 +616,12 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
     a.token_cap = s->tok_cap;
     a.last_token = s->last_tok;
     a.trace = take_slot(s);
+    if (fused) {
+        a.key_ctl = reinterpret_cast<uint32_t*>(s->peers.base[s->tp_rank] + h.tp.tp_off +
+                                                (size_t)2 * s->tp_world * s->peer_slice * 4 +
+                                                (size_t)2 * s->tp_world * GEMV_TP_MAX_CTAS * 4);
+        a.key_world = s->tp_world;
+    }
     return launch_ex(advance_kernel, dim3(1), dim3(32), 0, st, true, a);
 }
 
@@ -590,8 +632,9 @@ static q_error_code capture(DevState* s, float* kv, bool with_head, cudaGraphExe
     const uint64_t before = g_kernel_launches.load();
     if (!cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture"))
         return Q_ERR_INVALID_ARG;
-    cudaError_t e = enqueue_layers(s, kv, st);
-    if (e == cudaSuccess && with_head) e = enqueue_head(s, st, nullptr, sample);
+    const bool head_recv = with_head && tp_fused(s);
+    cudaError_t e = enqueue_layers(s, kv, st, head_recv);
+    if (e == cudaSuccess && with_head) e = enqueue_head(s, st, nullptr, sample, head_recv);
     cudaError_t e2 = cudaStreamEndCapture(st, &g);
     *n_kernels = g_kernel_launches.load() - before;
     g_kernel_launches.fetch_sub(*n_kernels);  // captured, not launched

@@ -99,3 +99,83 @@ def test_tp2_tiny_matches_upstream_and_oracle(tiny_path, golden, ipc, fused):
         assert (err <= np.maximum(1.5e-4, 1e-4 * np.abs(ref))).all(), f"kv worst {err.max():.3e}"
     assert res[0][6] == res[1][6]  # device-fed decode agrees across ranks
     orc.close()
+
+
+# ---- 2, 4 and 8 ranks on a config whose heads split 8 ways ---------------------
+
+WIDE = dict(vocab=1000, dim=512, hidden=1536, layers=2, heads=8, kv_heads=8, max_seq=256)
+
+
+def _wide_worker(rank, world, port, path, prompt, feed, fused, out):
+    os.environ["QORUS_B200_TP_FUSED"] = "1" if fused else "0"
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        box = [Q.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+
+        def gather(b):
+            allb = [None] * world
+            dist.all_gather_object(allb, b)
+            return allb
+        m = Q.Model(path, tp=(rank, world, box[0]), tp_gather=gather)
+        logits = [m.forward(prompt, 0).copy()]
+        for i, t in enumerate(feed):
+            logits.append(m.forward(np.array([t], np.uint32), len(prompt) + i).copy())
+        loop = m.decode_loop(int(feed[-1]), len(prompt) + len(feed), 12).tolist()
+        out.put((rank, np.stack(logits), loop))
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "kernel"])
+def test_tp_wide_matches_oracle(tmp_path, world, fused):
+    """Logits of a prompt and 15 fed tokens on `world` ranks against the CPU
+    oracle (max-abs <= 1e-2), and the device-fed greedy loop (argmax keys
+    exchanged between ranks) equal on every rank and to one GPU's loop."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    cfg = Q.config(**WIDE)
+    path = str(tmp_path / "wide.qorus")
+    Q.write_model(path, cfg, seed=7, threads=8)
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, WIDE["vocab"], 40).astype(np.uint32)
+    orc = O.OracleModel(path)
+    ref = [orc.forward(prompt, 0).copy()]
+    feed = []
+    for i in range(15):
+        feed.append(int(np.argmax(ref[-1])))
+        ref.append(orc.forward(np.array([feed[-1]], np.uint32), len(prompt) + i).copy())
+    orc.close()
+    solo = Q.Model(path)
+    solo.forward(prompt, 0)
+    for i, t in enumerate(feed):
+        solo.forward(np.array([t], np.uint32), len(prompt) + i)
+    solo_loop = solo.decode_loop(feed[-1], len(prompt) + len(feed), 12).tolist()
+    solo.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_wide_worker, args=(r, world, port, path, prompt, feed, fused, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r = q.get(timeout=300)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank in range(world):
+        _, lg, loop = res[rank]
+        err = np.abs(lg[:, : WIDE["vocab"]] - np.stack(ref)).max()
+        assert err <= LOGIT_TOL, f"rank {rank}: logits max-abs {err:.3e}"
+        assert loop == solo_loop, (rank, loop, solo_loop)
