@@ -342,7 +342,8 @@ q_error_code q_b200_selftest_exchange_timeout(uint64_t limit_ns, uint32_t* statu
     if (!status_out || limit_ns == 0) return Q_ERR_INVALID_ARG;
     *status_out = 0;
     // A single-rank receive of the fused tensor-parallel exchange whose
-    // sender never runs: every CTA's flag wait must give up after limit_ns.
+    // sender never runs: every CTA's wait for the tagged words must give up
+    // after limit_ns.
     GemvPlan p;
     ChainPlan cp;
     if (!plan_single(64, 256, p, cp)) return Q_ERR_INVALID_SIZE;
@@ -374,7 +375,6 @@ q_error_code q_b200_selftest_exchange_timeout(uint64_t limit_ns, uint32_t* statu
     t.tp_rank = 0;
     t.tp_recv = 1;
     t.tp_par = 0;
-    t.tp_expect = 1;
     const GemvPlan* m[1] = {&p};
     const cudaError_t e = launch_chain(cp, m, &a, scratch, nullptr, nullptr, st, false, &t);
     const cudaError_t e2 = cudaStreamSynchronize(st);

@@ -68,7 +68,6 @@ struct AttnArgs {
     // per sequence, and sequence b's cache planes follow the first b caches
     uint32_t seq_stride;     // floats of q / out per sequence
     uint32_t n_layers;       // planes per sequence = n_layers * n_kv_heads
-    L2Range l2pf[2];         // weights of later kernels, pulled into L2 while this one runs
 };
 
 // ring[slots][16 KB] | sc[G][chunk_alloc] | ored[PG][G][hd]
@@ -169,12 +168,6 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
     if (warp == NW) {
         // ---- producer: K rows of the chunk, then its V rows ------------------
         cluster_arrive();  // barrier 1 does not wait for the producer's copies
-        if (lane == 0) {
-            const uint32_t me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
-                           all = gridDim.x * gridDim.y * gridDim.z;
-            l2_prefetch_share(a.l2pf[0], me, all);
-            l2_prefetch_share(a.l2pf[1], me, all);
-        }
         const uint64_t pol = l2_evict_first_policy();
         uint32_t s = 0, ph = 0, k = 0;
         bool waited = false, ok = true;

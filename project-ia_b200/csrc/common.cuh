@@ -132,27 +132,6 @@ __device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
 // Both addresses 16-byte aligned, size a multiple of 16 (checked by callers).
 // Source is always this GPU's own memory; no multicast.
 
-// A byte range for a kernel to pull into L2 ahead of the kernel that reads
-// it (the decode chain's weights do not depend on activations, so they can
-// be fetched while a latency-bound kernel leaves HBM idle).
-struct L2Range {
-    const uint8_t* p;
-    uint32_t bytes;  // multiple of 16, p 16-byte aligned
-};
-
-// This CTA's share of r (256-byte aligned pieces of at most 64 KB), issued
-// by the calling thread as bulk L2 prefetches: no shared memory, nothing to
-// wait for.  This GPU's own memory.
-__device__ __forceinline__ void l2_prefetch_share(const L2Range& r, uint32_t cta, uint32_t ctas) {
-    if (!r.p || !r.bytes) return;
-    const uint32_t per = ((r.bytes + ctas - 1) / ctas + 255u) & ~255u;
-    const uint64_t b0 = (uint64_t)per * cta, e = min((uint64_t)r.bytes, b0 + per);
-    for (uint64_t b = b0; b < e; b += 65536) {
-        const uint32_t n = (uint32_t)min((uint64_t)65536, e - b);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r.p + b), "r"(n) : "memory");
-    }
-}
-
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

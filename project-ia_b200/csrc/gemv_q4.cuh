@@ -100,77 +100,125 @@ struct GemvArgs {
 
 // Tensor-parallel exchange fused into the GEMVs (peer memory).  Each
 // rank's exchange area (at byte tp_off of every rank's buffer) holds
-// recv[2][W][tp_slice] fp32 | flag[2][W][GEMV_TP_MAX_CTAS] | ticket[2] |
-// seq[2] u32 (seq[p]: receives of parity p this rank has completed).
-//   tp_send: the epilogue stores the finished rows (plus the residual on
-//   the rank whose epilogue adds it) into recv[tp_par][rank][row] of every
-//   rank instead of y, and CTA c, once its rows are stored, sets
-//   flag[tp_par][rank][c] = seq[tp_par] + 1 on every rank (release, system
-//   scope; one word per CTA, so no two CTAs write the same remote word);
-//   tp_recv: every CTA's prologue waits (bounded) until the tp_expect flags
-//   of parity tp_par (W ranks x the sending grid) reach seq[tp_par] + 1;
-//   the last CTA past the wait (local ticket) advances seq[tp_par]; each
-//   CTA then takes the input as the sum of the W slots in rank order (the
-//   bits a one-shot all-reduce would give).  Every rank runs the same
-//   exchanges, so the counts agree.  A slot is written again only by the
-//   next exchange of the same parity, whose send follows (in every rank's
-//   stream order) the receive of the exchange in between.
+// word[2][W][tp_slice] u64 | control words (256 bytes).  A word is
+// (sequence << 32) | fp32 bits, written with one 8-byte store (single-copy
+// atomic), so a value and its readiness travel together: the sender needs
+// no fence and no flag, the receiver polls the words themselves (the
+// low-latency protocol of NCCL's LL transport).  seq[p] in the control
+// words is this rank's count of completed receives of parity p; every rank
+// runs the same exchanges, so the counts agree.
+//   tp_send: the epilogue stores each finished row (plus the residual on the
+//   rank whose epilogue adds it) as word[tp_par][rank][row] of every rank,
+//   tagged seq[tp_par] + 1, instead of y;
+//   tp_recv: every CTA reads the W slots of parity tp_par, waiting (bounded)
+//   until each word carries seq[tp_par] + 1, and takes the input as their sum
+//   in rank order (the bits a one-shot all-reduce gives); the last CTA done
+//   reading (local ticket) advances seq[tp_par].  A slot is written again
+//   only by the next exchange of the same parity, whose send follows (in
+//   every rank's stream order) the receive of the exchange in between.
 struct GemvTp {
     uint8_t* tp_base[8];       // every rank's exchange buffer, mapped here
     uint32_t tp_off, tp_slice, tp_world, tp_rank;
-    uint32_t tp_send, tp_recv, tp_par, tp_expect;
+    uint32_t tp_send, tp_recv, tp_par;
 };
 
-static constexpr uint32_t GEMV_TP_MAX_CTAS = 256;  // flag words per (parity, rank)
+// Control words (u32 index from the control base): ticket[2] | seq[2] |
+// head ticket | key seq | 10 spare | key word[8][2] (u64 at u32 index 16:
+// the LM head's argmax key of each rank as two tagged halves).
+static constexpr uint32_t TP_CTL_HEAD_TICKET = 4, TP_CTL_KEY_SEQ = 5, TP_CTL_KEY = 16;
 
-// Control words after the flags (u32 index from the control base):
-// ticket[2] | seq[2] | head ticket | key seq | 2 spare | key flag[8] |
-// key[8] (u64, the LM head's argmax key of each rank).
-static constexpr uint32_t TP_CTL_HEAD_TICKET = 4, TP_CTL_KEY_SEQ = 5, TP_CTL_KEY_FLAG = 8, TP_CTL_KEY = 16;
-
-__device__ __forceinline__ uint32_t* tp_flag_base(const GemvTp& t, uint32_t rank) {
-    return reinterpret_cast<uint32_t*>(t.tp_base[rank] + t.tp_off + (size_t)2 * t.tp_world * t.tp_slice * 4);
+__device__ __forceinline__ uint64_t* tp_words(const GemvTp& t, uint32_t rank) {
+    return reinterpret_cast<uint64_t*>(t.tp_base[rank] + t.tp_off);
 }
 __device__ __forceinline__ uint32_t* tp_ctl(const GemvTp& t, uint32_t rank) {
-    return tp_flag_base(t, rank) + (size_t)2 * t.tp_world * GEMV_TP_MAX_CTAS;
+    return reinterpret_cast<uint32_t*>(tp_words(t, rank) + (size_t)2 * t.tp_world * t.tp_slice);
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_relaxed_sys_u64x2(const uint64_t* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t tp_word(uint32_t seq, float v) {
+    return ((uint64_t)seq << 32) | __float_as_uint(v);
 }
 
-// Receive side of an exchange of parity t.tp_par, run by the T threads of
-// named barrier 1 in every CTA of the grid: wait (bounded) until the
-// t.tp_expect flags (W ranks x the sending grid) carry this exchange's
-// sequence number — this rank's count of completed receives of the parity,
-// plus one — then the last CTA past the wait (local ticket) advances the
-// count.  Nothing is cleared, so a flag that lands late (after a timed-out
-// wait) is below the next exchange's number and cannot release it.
-// Returns this rank's receive slots of the parity, [W][tp_slice] fp32.
-__device__ __forceinline__ const float* tp_recv_wait(const GemvTp& t, uint32_t tid, uint32_t T) {
-    const uint32_t* flag = tp_flag_base(t, t.tp_rank) + (size_t)t.tp_par * t.tp_world * GEMV_TP_MAX_CTAS;
-    uint32_t* ctl = tp_ctl(t, t.tp_rank);
-    uint32_t* ticket = ctl + t.tp_par;
-    uint32_t* seqw = ctl + 2 + t.tp_par;
-    const uint32_t want = __ldcg(seqw) + 1u;
-    const uint32_t per = t.tp_expect / t.tp_world;
-    const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
-    for (uint32_t i = tid; i < t.tp_expect; i += T) {
-        const uint32_t* f = flag + (size_t)(i / per) * GEMV_TP_MAX_CTAS + i % per;
-        while ((int32_t)(ld_acquire_sys(f) - want) < 0) {
-            if (gtimer() - t0 > lim) {
+// Adds (first: stores) the float4s i = base + tid + T r (r < NR, i < n4) of
+// one received slot into xv, waiting for each word to carry `want`.  All
+// loads of the slot are issued before any is checked; a word that is not
+// there yet is polled again until it is or the wait (from t0) runs out —
+// once it has, no later word waits (late).
+template <int NR>
+__device__ __forceinline__ void tp_take(const uint64_t* slot, uint32_t base, uint32_t tid, uint32_t T,
+                                        uint32_t n4, uint32_t want, float4 (&xv)[NR], bool first,
+                                        unsigned long long t0, bool& late) {
+    ulonglong2 w[NR][2];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const uint32_t i = base + tid + T * r;
+        if (i < n4) {
+            w[r][0] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i);
+            w[r][1] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i + 2);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const uint32_t i = base + tid + T * r;
+        if (i >= n4) {
+            if (first) xv[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
+        while (!late && ((uint32_t)(w[r][0].x >> 32) != want || (uint32_t)(w[r][0].y >> 32) != want ||
+                         (uint32_t)(w[r][1].x >> 32) != want || (uint32_t)(w[r][1].y >> 32) != want)) {
+            if (gtimer() - t0 > qdev_wait_ns()) {
                 qdev_fail(QDEV_PEER_TIMEOUT);
-                break;
+                late = true;
+            } else {
+                w[r][0] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i);
+                w[r][1] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i + 2);
             }
         }
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(T));
-    if (tid == 0) {
-        uint32_t old;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
-        if (old == gridDim.x - 1) {  // every CTA has read `want`
-            *ticket = 0u;
-            __stcg(seqw, want);
+        const float4 v = make_float4(__uint_as_float((uint32_t)w[r][0].x), __uint_as_float((uint32_t)w[r][0].y),
+                                     __uint_as_float((uint32_t)w[r][1].x), __uint_as_float((uint32_t)w[r][1].y));
+        if (first) {
+            xv[r] = v;
+        } else {
+            xv[r].x += v.x;
+            xv[r].y += v.y;
+            xv[r].z += v.z;
+            xv[r].w += v.w;
         }
     }
-    return reinterpret_cast<const float*>(t.tp_base[t.tp_rank] + t.tp_off) +
-           (size_t)t.tp_par * t.tp_world * t.tp_slice;
+}
+
+// The input float4s of one tp_take pass, summed over the W slots in rank order.
+// (In groups of 4 float4s: 16 words in flight per thread keeps the
+// receiving GEMV within its register budget.)
+template <int NR>
+__device__ __forceinline__ void tp_take_all(const GemvTp& t, uint32_t base, uint32_t tid, uint32_t T, uint32_t n4,
+                                            uint32_t want, float4 (&xv)[NR], unsigned long long t0, bool& late) {
+    static_assert(NR % 4 == 0, "groups of 4");
+    const uint64_t* mine = tp_words(t, t.tp_rank) + (size_t)t.tp_par * t.tp_world * t.tp_slice;
+#pragma unroll
+    for (int g = 0; g < NR / 4; ++g) {
+        float4(&xg)[4] = *reinterpret_cast<float4(*)[4]>(&xv[4 * g]);
+        for (uint32_t q = 0; q < t.tp_world; ++q)
+            tp_take<4>(mine + (size_t)q * t.tp_slice, base + 4 * g * T, tid, T, n4, want, xg, q == 0, t0, late);
+    }
+}
+
+// After every thread of this CTA has read the exchange (call after a CTA
+// barrier, one thread): the last CTA of the grid advances the count.
+__device__ __forceinline__ void tp_recv_done(const GemvTp& t, uint32_t want) {
+    uint32_t* ctl = tp_ctl(t, t.tp_rank);
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctl + t.tp_par) : "memory");
+    if (old == gridDim.x - 1) {  // every CTA has read `want` and its words
+        ctl[t.tp_par] = 0u;
+        __stcg(ctl + 2 + t.tp_par, want);
+    }
 }
 
 // A chain of up to GEMV_MAX_PHASES GEMVs run by one persistent grid: phase
@@ -188,7 +236,6 @@ struct GemvChain {
     uint32_t* bar;              // n_phases counters, zero between launches (n_phases > 1)
     unsigned long long* trace;  // step-trace slot (null: off)
     GemvTp tp;                  // single-phase launches of q4_slab_kernel<true> only
-    L2Range l2pf[2];            // weights of later kernels, pulled into L2 while this one runs
 };
 
 // Shared memory: ring | bfrag[max_nb][144] | fsc[max_nb][4] float2 | red[red_slabs][NW][32] | bars | misc
@@ -233,16 +280,17 @@ __device__ __forceinline__ void mma_u8s8(int d[4], uint32_t a0, uint32_t a1, uin
 // Epilogue for lanes 0..15 of one warp holding the 16 finished rows of slab j
 // (lane = row within the slab).  Pairs use the odd lane's value via shuffle.
 template <bool TP>
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const GemvTp& tpa, uint32_t j, uint32_t lane,
-                                              float v) {
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const GemvTp& tpa, uint32_t tp_seq, uint32_t j,
+                                              uint32_t lane, float v) {
     const float vn = __shfl_down_sync(0xffffffffu, v, 1);
     const uint32_t row = j * GEMV_SLAB_ROWS + lane;
     if (row >= a.M) return;
     if constexpr (TP) {
-        if (tpa.tp_send) {  // EPI_STORE / EPI_RESID rows to every rank's receive slot
+        if (tpa.tp_send) {  // EPI_STORE / EPI_RESID rows, tagged, to every rank's receive slot
             const float o = a.epi == EPI_RESID ? __fadd_rn(__ldcg(&a.resid[row]), v) : v;
-            const size_t at = tpa.tp_off + (((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * tpa.tp_slice + row) * 4;
-            for (uint32_t r = 0; r < tpa.tp_world; ++r) *reinterpret_cast<float*>(tpa.tp_base[r] + at) = o;
+            const size_t at = ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * tpa.tp_slice + row;
+            const uint64_t w = tp_word(tp_seq, o);
+            for (uint32_t r = 0; r < tpa.tp_world; ++r) st_relaxed_sys_u64(tp_words(tpa, r) + at, w);
             return;
         }
     }
@@ -347,12 +395,15 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     const float4* g4 = reinterpret_cast<const float4*>(a.norm_w);
     constexpr int NR = 8;
     float r_norm = 1.0f;
-    const float4* rx4 = nullptr;  // tensor-parallel receive slots of this exchange, [W][tp_slice]
     const GemvTp& tpa = c.tp;
-    if (TP && tpa.tp_recv) rx4 = reinterpret_cast<const float4*>(tp_recv_wait(tpa, tid, T));
+    // tensor parallel: this exchange's sequence number (receive: the tag the
+    // words must carry; send: the tag they get)
+    const uint32_t tp_seq = TP && (tpa.tp_recv || tpa.tp_send) ? __ldcg(tp_ctl(tpa, tpa.tp_rank) + 2 + tpa.tp_par) + 1u : 0u;
+    const unsigned long long tp_t0 = TP && tpa.tp_recv ? gtimer() : 0ull;
+    bool tp_late = false;
     for (uint32_t base = 0; base < n4; base += T * NR) {
         float4 xv[NR];
-        if (!TP || !rx4) {
+        if (!TP || !tpa.tp_recv) {
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
                 const uint32_t i = base + tid + T * r;
@@ -361,25 +412,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         } else {
             // the W received slots, added in rank order as the one-shot
             // all-reduce adds them
-#pragma unroll
-            for (int r = 0; r < NR; ++r) {
-                const uint32_t i = base + tid + T * r;
-                xv[r] = i < n4 ? __ldcg(rx4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            for (uint32_t q = 1; q < tpa.tp_world; ++q) {
-                const float4* src = rx4 + (size_t)q * (tpa.tp_slice / 4);
-#pragma unroll
-                for (int r = 0; r < NR; ++r) {
-                    const uint32_t i = base + tid + T * r;
-                    if (i < n4) {
-                        const float4 t4 = __ldcg(src + i);
-                        xv[r].x += t4.x;
-                        xv[r].y += t4.y;
-                        xv[r].z += t4.z;
-                        xv[r].w += t4.w;
-                    }
-                }
-            }
+            tp_take_all<NR>(tpa, base, tid, T, n4, tp_seq, xv, tp_t0, tp_late);
         }
         if (a.x_copy && cta == 0 && !dry) {
 #pragma unroll
@@ -434,6 +467,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(T));
+    if (TP && tpa.tp_recv && tid == 0) tp_recv_done(tpa, tp_seq);
     for (uint32_t b = tid; b < nbk; b += T) {
         float v[32];
         const uint8_t* src = bfrag + (size_t)b * GEMV_BFRAG_BYTES;
@@ -577,7 +611,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
                     finish = true;
                 }
             }
-            if (finish) gemv_epilogue<TP>(a, c.tp, j, lane, v);
+            if (finish) gemv_epilogue<TP>(a, c.tp, tp_seq, j, lane, v);
         }
         j_batch += cnt;
         jl = 0;
@@ -653,16 +687,6 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& a, const GemvChain& c
     }
     if (jl) reduce_batch(jl);
     asm volatile("bar.sync 1, %0;" ::"r"(T));  // tables and red[] free for the next phase
-    if (TP && tpa.tp_send && tid < tpa.tp_world) {
-        // every row this CTA finished is stored (bar.sync above): publish to
-        // rank tid
-        // (flag value: this exchange's sequence number, from this rank's
-        // own receive count of the parity; every rank counts the same)
-        const uint32_t seq = __ldcg(tp_ctl(tpa, tpa.tp_rank) + 2 + tpa.tp_par) + 1u;
-        __threadfence_system();
-        st_release_sys(tp_flag_base(tpa, tid) + ((size_t)tpa.tp_par * tpa.tp_world + tpa.tp_rank) * GEMV_TP_MAX_CTAS + cta,
-                       seq);
-    }
 }
 
 // TP: the single-phase tensor-parallel form (c.tp: exchange fused into
@@ -710,8 +734,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1)
     if (tid >= T) {
         // ---- producer warp: every phase's block range, back to back ----------
         if (tid == T) {
-            l2_prefetch_share(c.l2pf[0], cta, G);
-            l2_prefetch_share(c.l2pf[1], cta, G);
             const uint64_t pol = l2_evict_first_policy();
             uint32_t s = 0, ph = 0, k = 0;  // ring slot, its parity, stages issued
             bool ok = true;

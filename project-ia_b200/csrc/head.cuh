@@ -39,9 +39,9 @@ struct HeadArgs {
     //   slots of parity tp.tp_par that the last layer's down projection sent,
     //   and CTA 0 stores that sum (the residual stream) to x_copy;
     //   tp_key: once every CTA has folded its rows into *best (local ticket),
-    //   the last CTA stores the key to key[rank] of every rank and raises
-    //   key_flag[rank] to the key exchange's sequence number; advance_kernel
-    //   takes the maximum of the W keys.
+    //   the last CTA stores the key as key word[rank][0..1] of every rank (low
+    //   and high halves, each tagged with the key exchange's sequence number);
+    //   advance_kernel takes the maximum of the W keys.
     GemvTp tp;
     float* x_copy;
     uint32_t tp_key;
@@ -124,17 +124,31 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs
     pdl_wait();
     if (tid == 0) trace_mark(a.trace, 1);
     if (a.tp.tp_recv) {
-        const float* rx = tp_recv_wait(a.tp, tid, T);
-        for (uint32_t i = tid; i < K; i += T) {
-            float v = __ldcg(rx + i);  // the W slots in rank order, as the one-shot all-reduce adds them
-            for (uint32_t q = 1; q < a.tp.tp_world; ++q) v = __fadd_rn(v, __ldcg(rx + (size_t)q * a.tp.tp_slice + i));
-            xs[i] = v;
-            if (a.x_copy && blockIdx.x == 0) a.x_copy[i] = v;
+        // the W slots in rank order, as the one-shot all-reduce adds them
+        const uint32_t want = __ldcg(tp_ctl(a.tp, a.tp.tp_rank) + 2 + a.tp.tp_par) + 1u;
+        const unsigned long long t0 = gtimer();
+        bool late = false;
+        constexpr int NR = 4;
+        const uint32_t n4 = K / 4;
+        for (uint32_t base = 0; base < n4; base += T * NR) {
+            float4 xv[NR];
+            tp_take_all<NR>(a.tp, base, tid, T, n4, want, xv, t0, late);
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const uint32_t i = base + tid + T * r;
+                if (i < n4) {
+                    reinterpret_cast<float4*>(xs)[i] = xv[r];
+                    if (a.x_copy && blockIdx.x == 0) reinterpret_cast<float4*>(a.x_copy)[i] = xv[r];
+                }
+            }
         }
+        asm volatile("bar.sync 1, %0;" ::"r"(T));
+        if (tid == 0) tp_recv_done(a.tp, want);
     } else {
         for (uint32_t i = tid; i < K; i += T) xs[i] = a.x[i];
     }
-    // (each thread normalises the elements it stored, so no barrier yet)
+    // (without a receive each thread normalises the elements it stored, so
+    // no barrier is needed yet)
     float r = 1.0f;
     if (a.norm_w) {
         float ss = 0.0f;
@@ -226,11 +240,11 @@ __global__ void __launch_bounds__(HEAD_THREADS, 1) lm_head_kernel(const HeadArgs
                 ctl[TP_CTL_HEAD_TICKET] = 0u;
                 const unsigned long long k = atomicAdd(a.best, 0ull);
                 const uint32_t seq = __ldcg(ctl + TP_CTL_KEY_SEQ) + 1u;
-                for (uint32_t q = 0; q < a.tp.tp_world; ++q)
-                    *reinterpret_cast<volatile unsigned long long*>(tp_ctl(a.tp, q) + TP_CTL_KEY + 2 * a.tp.tp_rank) = k;
-                __threadfence_system();
-                for (uint32_t q = 0; q < a.tp.tp_world; ++q)
-                    st_release_sys(tp_ctl(a.tp, q) + TP_CTL_KEY_FLAG + a.tp.tp_rank, seq);
+                for (uint32_t q = 0; q < a.tp.tp_world; ++q) {
+                    uint64_t* kw = reinterpret_cast<uint64_t*>(tp_ctl(a.tp, q) + TP_CTL_KEY) + 2 * a.tp.tp_rank;
+                    st_relaxed_sys_u64(kw, ((uint64_t)seq << 32) | (uint32_t)k);
+                    st_relaxed_sys_u64(kw + 1, ((uint64_t)seq << 32) | (uint32_t)(k >> 32));
+                }
             }
         }
         trace_mark(a.trace, 2);
@@ -262,15 +276,17 @@ __global__ void advance_kernel(const AdvanceArgs a) {
         const uint32_t want = __ldcg(a.key_ctl + TP_CTL_KEY_SEQ) + 1u;
         const unsigned long long t0 = gtimer(), lim = qdev_wait_ns();
         k = 0ull;
+        const uint64_t* kw = reinterpret_cast<const uint64_t*>(a.key_ctl + TP_CTL_KEY);
         for (uint32_t q = 0; q < a.key_world; ++q) {
-            while ((int32_t)(ld_acquire_sys(a.key_ctl + TP_CTL_KEY_FLAG + q) - want) < 0) {
+            ulonglong2 w = ld_relaxed_sys_u64x2(kw + 2 * q);
+            while ((uint32_t)(w.x >> 32) != want || (uint32_t)(w.y >> 32) != want) {
                 if (gtimer() - t0 > lim) {
                     qdev_fail(QDEV_PEER_TIMEOUT);
                     break;
                 }
+                w = ld_relaxed_sys_u64x2(kw + 2 * q);
             }
-            const unsigned long long v =
-                *reinterpret_cast<volatile const unsigned long long*>(a.key_ctl + TP_CTL_KEY + 2 * q);
+            const unsigned long long v = ((unsigned long long)(uint32_t)w.y << 32) | (uint32_t)w.x;
             k = v > k ? v : k;
         }
         __stcg(a.key_ctl + TP_CTL_KEY_SEQ, want);

@@ -356,11 +356,8 @@ static q_error_code make_kv_map(DevState* s, void* kv) {
     return Q_OK;
 }
 
-static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t st, L2Range pf0 = {},
-                                     L2Range pf1 = {}) {
+static cudaError_t enqueue_attention(DevState* s, uint32_t layer, cudaStream_t st) {
     AttnArgs a{};
-    a.l2pf[0] = pf0;
-    a.l2pf[1] = pf1;
     a.q = s->q;
     a.layer = layer;
     a.trace = take_slot(s);
@@ -448,7 +445,6 @@ static cudaError_t allreduce_sum(DevState* s, float* buf, size_t count, cudaStre
 // and sum them.  Parity 0 carries wo's exchange, parity 1 down's.
 static bool tp_fused(const DevState* s) {
     if (s->tp_world < 2 || !s->peers_ready) return false;
-    if (s->cp_wo.grid > GEMV_TP_MAX_CTAS || s->cp_down.grid > GEMV_TP_MAX_CTAS) return false;
     const char* e = getenv("QORUS_B200_TP_FUSED");
     return !(e && e[0] == '0');
 }
@@ -459,38 +455,27 @@ static void tp_geometry(const DevState* s, GemvTp& t) {
     t.tp_world = s->tp_world;
     t.tp_rank = s->tp_rank;
 }
-static void tp_fuse(const DevState* s, GemvArgs& g, GemvTp& t, bool send, uint32_t par, uint32_t expect) {
+static void tp_fuse(const DevState* s, GemvArgs& g, GemvTp& t, bool send, uint32_t par) {
     tp_geometry(s, t);
     t.tp_par = par;
     if (send) {
         t.tp_send = 1;
     } else {
         t.tp_recv = 1;
-        t.tp_expect = expect;
         g.x_copy = s->x;  // CTA 0 stores the summed input: the residual stream
     }
 }
 
 // head_recv: the LM head follows and takes the last layer's down exchange
 // itself (fused tensor-parallel exchange only).
-static L2Range l2_slice(const uint8_t* w, size_t total, double off_mb, double mb) {
-    const size_t off = std::min(total, (size_t)(off_mb * 1048576.0) / 256 * 256);
-    const size_t n = std::min(total - off, (size_t)(mb * 1048576.0) / 256 * 256);
-    return n ? L2Range{w + off, (uint32_t)n} : L2Range{};
-}
-
 static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st, bool head_recv = false) {
     const q_llama_config& c = s->cfg;
-    double kn[5] = {0, 0, 0, 0, 0};  // EXPERIMENT: att_wo, att_gu, wo_gu, gu_down, down_qkv (MB)
-    if (const char* e = getenv("QB_EXP_L2PF"))
-        sscanf(e, "%lf,%lf,%lf,%lf,%lf", &kn[0], &kn[1], &kn[2], &kn[3], &kn[4]);
     const uint32_t D = c.dim;
     GemvArgs first = qkv_args(s, kv, 0);
     const GemvPlan* fm[1] = {&s->p_qkv};
     cudaError_t e = launch_chain(s->cp_first, fm, &first, s->gemv_scratch, nullptr, take_slot(s), st, false);
     for (uint32_t l = 0; l < c.n_layers && e == cudaSuccess; ++l) {
-        e = enqueue_attention(s, l, st, l2_slice(s->wo[l], s->p_wo.packed_bytes, 0, kn[0]),
-                              l2_slice(s->gu[l], s->p_gu.packed_bytes, 0, kn[1]));
+        e = enqueue_attention(s, l, st);
         if (e != cudaSuccess) break;
         GemvArgs ph[4] = {};
         ph[0].w = s->wo[l];  // attention output -> residual
@@ -514,18 +499,14 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st, bool 
         ph[2].epi = residual_epi(s);
         const bool more = l + 1 < c.n_layers;
         if (more) ph[3] = qkv_args(s, kv, l + 1);
-        const L2Range pfs[4] = {l2_slice(s->gu[l], s->p_gu.packed_bytes, kn[1], kn[2]),
-                                l2_slice(s->down[l], s->p_down.packed_bytes, 0, kn[3]),
-                                more ? l2_slice(s->qkv[l + 1], s->p_qkv.packed_bytes, 0, kn[4]) : L2Range{},
-                                L2Range{}};
         GemvTp tps[4] = {};
         if (tp_fused(s)) {
-            tp_fuse(s, ph[0], tps[0], true, 0, 0);
-            tp_fuse(s, ph[1], tps[1], false, 0, s->cp_wo.grid * s->tp_world);
+            tp_fuse(s, ph[0], tps[0], true, 0);
+            tp_fuse(s, ph[1], tps[1], false, 0);
             // the last layer's down feeds the LM head's prologue, or (rows
             // without a head) the all-reduce kernel
-            if (more || head_recv) tp_fuse(s, ph[2], tps[2], true, 1, 0);
-            if (more) tp_fuse(s, ph[3], tps[3], false, 1, s->cp_down.grid * s->tp_world);
+            if (more || head_recv) tp_fuse(s, ph[2], tps[2], true, 1);
+            if (more) tp_fuse(s, ph[3], tps[3], false, 1);
         }
         const GemvPlan* mats[4] = {&s->p_wo, &s->p_gu, &s->p_down, &s->p_qkv};
         if (s->chain_phases > 1) {
@@ -536,7 +517,7 @@ static cudaError_t enqueue_layers(DevState* s, float* kv, cudaStream_t st, bool 
             const ChainPlan* one[4] = {&s->cp_wo, &s->cp_gu, &s->cp_down, &s->cp_first};
             for (uint32_t i = 0; i < (more ? 4u : 3u) && e == cudaSuccess; ++i) {
                 e = launch_chain(*one[i], &mats[i], &ph[i], s->gemv_scratch, nullptr, take_slot(s), st, true,
-                                 &tps[i], pfs[i]);
+                                 &tps[i]);
                 // wo and down hold partial residual updates on a tensor-parallel rank
                 if (e == cudaSuccess && (i == 0 || i == 2) && !tps[i].tp_send) e = allreduce_sum(s, s->x, c.dim, st);
             }
@@ -559,7 +540,6 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
         if (tp_recv) {
             h.tp.tp_recv = 1;
             h.tp.tp_par = 1;
-            h.tp.tp_expect = s->cp_down.grid * s->tp_world;
             h.x_copy = s->x;
         }
     }
@@ -618,8 +598,7 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
     a.trace = take_slot(s);
     if (fused) {
         a.key_ctl = reinterpret_cast<uint32_t*>(s->peers.base[s->tp_rank] + h.tp.tp_off +
-                                                (size_t)2 * s->tp_world * s->peer_slice * 4 +
-                                                (size_t)2 * s->tp_world * GEMV_TP_MAX_CTAS * 4);
+                                                (size_t)2 * s->tp_world * s->peer_slice * 8);
         a.key_world = s->tp_world;
     }
     return launch_ex(advance_kernel, dim3(1), dim3(32), 0, st, true, a);

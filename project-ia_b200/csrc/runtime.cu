@@ -199,10 +199,8 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp) {
 
 cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const GemvArgs* args,
                          void* scratch, uint32_t* bar, unsigned long long* trace, cudaStream_t s,
-                         bool pdl, const GemvTp* tp, L2Range pf0, L2Range pf1) {
+                         bool pdl, const GemvTp* tp) {
     GemvChain c{};
-    c.l2pf[0] = pf0;
-    c.l2pf[1] = pf1;
     for (uint32_t i = 0; i < cp.n; ++i) {
         GemvArgs a = args[i];
         a.M = mats[i]->M;

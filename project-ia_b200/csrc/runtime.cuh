@@ -82,7 +82,7 @@ bool plan_chain(const GemvPlan* const* mats, uint32_t n, ChainPlan& cp);
 // cp.n zeroed counters when cp.n > 1 (likewise left zero).
 cudaError_t launch_chain(const ChainPlan& cp, const GemvPlan* const* mats, const GemvArgs* args,
                          void* scratch, uint32_t* bar, unsigned long long* trace, cudaStream_t s,
-                         bool pdl, const GemvTp* tp = nullptr, L2Range pf0 = {}, L2Range pf1 = {});
+                         bool pdl, const GemvTp* tp = nullptr);
 // One GEMV on its own (a one-phase chain).
 bool plan_single(uint32_t M, uint32_t K, GemvPlan& p, ChainPlan& cp);
 cudaError_t launch_single(const ChainPlan& cp, const GemvPlan& p, const GemvArgs& a, void* scratch,

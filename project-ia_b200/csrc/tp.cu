@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(512) tp_allreduce_kernel(const TpArgs a) {
     constexpr uint32_t T = 512;
     const uint32_t tid = threadIdx.x, W = a.world, me = a.rank;
     __shared__ uint32_t seq;
-    pdl_wait();  // the input is the previous kernel's output
+    pdl_trigger();  // the next kernel may start streaming its weights
+    pdl_wait();     // the input is the previous kernel's output
     uint8_t* mine = a.peers.base[me];
     const size_t slice = (size_t)a.slice * 4;
     uint32_t* myflags = reinterpret_cast<uint32_t*>(mine + 2 * W * slice);

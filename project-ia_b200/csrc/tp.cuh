@@ -63,14 +63,13 @@ const NcclApi* nccl();
 // passed the all-reduce in between.
 static constexpr uint32_t TP_MAX_RANKS = 8;
 // Byte offset of the exchange area the GEMVs use directly (GemvArgs::tp_*):
-// recv[2][W][slice] fp32 | flag[2][W][256] u32 (GEMV_TP_MAX_CTAS) | control
-// words (ticket[2] | seq[2] | head ticket | key seq | key flag[8] | key[8] u64,
-// 256 bytes reserved).
+// word[2][W][slice] u64 (sequence-tagged fp32) | control words (ticket[2] |
+// seq[2] | head ticket | key seq | key words, 256 bytes reserved).
 inline size_t tp_fused_offset(uint32_t world, uint32_t slice) {
     return ((size_t)2 * world * slice * 4 + (size_t)2 * world * 4 + 256 + 255) / 256 * 256;
 }
 inline size_t tp_buffer_bytes(uint32_t world, uint32_t slice) {
-    return tp_fused_offset(world, slice) + (size_t)2 * world * slice * 4 + (size_t)2 * world * 256 * 4 + 256;
+    return tp_fused_offset(world, slice) + (size_t)2 * world * slice * 8 + 256;
 }
 
 struct TpPeers {
