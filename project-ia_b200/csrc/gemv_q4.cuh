@@ -145,67 +145,60 @@ __device__ __forceinline__ uint64_t tp_word(uint32_t seq, float v) {
     return ((uint64_t)seq << 32) | __float_as_uint(v);
 }
 
-// Adds (first: stores) the float4s i = base + tid + T r (r < NR, i < n4) of
-// one received slot into xv, waiting for each word to carry `want`.  All
-// loads of the slot are issued before any is checked; a word that is not
-// there yet is polled again until it is or the wait (from t0) runs out —
-// once it has, no later word waits (late).
-template <int NR>
-__device__ __forceinline__ void tp_take(const uint64_t* slot, uint32_t base, uint32_t tid, uint32_t T,
-                                        uint32_t n4, uint32_t want, float4 (&xv)[NR], bool first,
-                                        unsigned long long t0, bool& late) {
-    ulonglong2 w[NR][2];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const uint32_t i = base + tid + T * r;
-        if (i < n4) {
-            w[r][0] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i);
-            w[r][1] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i + 2);
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const uint32_t i = base + tid + T * r;
-        if (i >= n4) {
-            if (first) xv[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-            continue;
-        }
-        while (!late && ((uint32_t)(w[r][0].x >> 32) != want || (uint32_t)(w[r][0].y >> 32) != want ||
-                         (uint32_t)(w[r][1].x >> 32) != want || (uint32_t)(w[r][1].y >> 32) != want)) {
-            if (gtimer() - t0 > qdev_wait_ns()) {
-                qdev_fail(QDEV_PEER_TIMEOUT);
-                late = true;
-            } else {
-                w[r][0] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i);
-                w[r][1] = ld_relaxed_sys_u64x2(slot + 4 * (size_t)i + 2);
-            }
-        }
-        const float4 v = make_float4(__uint_as_float((uint32_t)w[r][0].x), __uint_as_float((uint32_t)w[r][0].y),
-                                     __uint_as_float((uint32_t)w[r][1].x), __uint_as_float((uint32_t)w[r][1].y));
-        if (first) {
-            xv[r] = v;
-        } else {
-            xv[r].x += v.x;
-            xv[r].y += v.y;
-            xv[r].z += v.z;
-            xv[r].w += v.w;
-        }
-    }
-}
-
-// The input float4s of one tp_take pass, summed over the W slots in rank order.
-// (In groups of 4 float4s: 16 words in flight per thread keeps the
-// receiving GEMV within its register budget.)
+// The input float4s i = base + tid + T r (r < NR, i < n4; zero past n4),
+// each the sum over the W received slots in rank order.  For one float4
+// the loads of up to 4 slots are issued before any is checked, so a receive
+// costs one round trip per float4 a thread takes (two at W = 8), not one
+// per rank; a word that is not there yet is polled again until it carries
+// `want` or the wait (from t0) runs out — once it has, no later word waits
+// (late).
 template <int NR>
 __device__ __forceinline__ void tp_take_all(const GemvTp& t, uint32_t base, uint32_t tid, uint32_t T, uint32_t n4,
                                             uint32_t want, float4 (&xv)[NR], unsigned long long t0, bool& late) {
-    static_assert(NR % 4 == 0, "groups of 4");
     const uint64_t* mine = tp_words(t, t.tp_rank) + (size_t)t.tp_par * t.tp_world * t.tp_slice;
+    const uint32_t W = t.tp_world;
 #pragma unroll
-    for (int g = 0; g < NR / 4; ++g) {
-        float4(&xg)[4] = *reinterpret_cast<float4(*)[4]>(&xv[4 * g]);
-        for (uint32_t q = 0; q < t.tp_world; ++q)
-            tp_take<4>(mine + (size_t)q * t.tp_slice, base + 4 * g * T, tid, T, n4, want, xg, q == 0, t0, late);
+    for (int r = 0; r < NR; ++r) {
+        const uint32_t i = base + tid + T * r;
+        xv[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i >= n4) continue;
+        for (uint32_t q0 = 0; q0 < W; q0 += 4) {  // 4 ranks' loads in flight (registers)
+            ulonglong2 w[4][2];
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+                if (q0 + k < W) {
+                    const uint64_t* p = mine + (size_t)(q0 + k) * t.tp_slice + 4 * (size_t)i;
+                    w[k][0] = ld_relaxed_sys_u64x2(p);
+                    w[k][1] = ld_relaxed_sys_u64x2(p + 2);
+                }
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+                const uint32_t q = q0 + k;
+                if (q >= W) continue;
+                const uint64_t* p = mine + (size_t)q * t.tp_slice + 4 * (size_t)i;
+                while (!late && ((uint32_t)(w[k][0].x >> 32) != want || (uint32_t)(w[k][0].y >> 32) != want ||
+                                 (uint32_t)(w[k][1].x >> 32) != want || (uint32_t)(w[k][1].y >> 32) != want)) {
+                    if (gtimer() - t0 > qdev_wait_ns()) {
+                        qdev_fail(QDEV_PEER_TIMEOUT);
+                        late = true;
+                    } else {
+                        w[k][0] = ld_relaxed_sys_u64x2(p);
+                        w[k][1] = ld_relaxed_sys_u64x2(p + 2);
+                    }
+                }
+                const float4 v = make_float4(__uint_as_float((uint32_t)w[k][0].x), __uint_as_float((uint32_t)w[k][0].y),
+                                             __uint_as_float((uint32_t)w[k][1].x), __uint_as_float((uint32_t)w[k][1].y));
+                if (q == 0) {
+                    xv[r] = v;
+                } else {
+                    xv[r].x += v.x;
+                    xv[r].y += v.y;
+                    xv[r].z += v.z;
+                    xv[r].w += v.w;
+                }
+            }
+        }
     }
 }
 
