@@ -318,6 +318,65 @@ def prefill_measure(Q, m, torch, peak_tf: float, reps: int = 3) -> dict:
             "reps": reps, "source": "llama_forward(2048 ids, pos 0) with host buffers"}
 
 
+CFG70B = dict(vocab=128256, dim=8192, hidden=28672, layers=80, heads=64, kv_heads=8)
+BATCH = 16
+
+
+def batch_measure(Q, torch, peak: float, steps: int = 16) -> dict:
+    """BASELINE configs[4] (Llama-3-70B, batch 16) on one GPU, measured per
+    layer: models with 2 and 4 layers of the 70B shapes (vocabulary cut to
+    4096 so the files stay small), 16 sequences each with its own cache
+    pre-filled to 2048 positions, q_b200_decode_batch_loop (argmax fed back
+    on the device) timed with CUDA events on the library stream.  One layer
+    = the difference of the two step times over 2; the 80-layer step is an
+    estimate: 80 layers measured + the 128256-row FP32 LM head at the
+    measured HBM peak."""
+    import ctypes as C
+    ms = {}
+    for L in (2, 4):
+        cfg = Q.config(4096, CFG70B["dim"], CFG70B["hidden"], L, CFG70B["heads"], CFG70B["kv_heads"], 2304)
+        p = str(Path(model_path(2304)).with_name(f"qorus_llama3_70b_{L}layer_v4096.qorus"))
+        if not (Path(p).exists() and Path(p).stat().st_size == int(Q.lib.q_b200_model_file_size(C.byref(cfg)))):
+            Q.write_model(p, cfg, seed=SEED, threads=0)
+        m = Q.Model(p)
+        Q.check(Q.lib.q_b200_batch_init(C.byref(m.ctx), C.byref(m.model), BATCH), "batch_init")
+        kv = np.zeros(L * CFG70B["kv_heads"] * 2304 * 256, np.float32)
+        for b in range(BATCH):
+            Q.check(Q.lib.q_b200_fill_kv_prefill(Q.ptr(kv), C.byref(cfg), PREFILL, SEED + b, 0), "fill_kv")
+            Q.check(Q.lib.q_b200_batch_kv_write(C.byref(m.ctx), b, 0, Q.ptr(kv), kv.nbytes), "batch_kv_write")
+        del kv
+        toks = np.arange(1, BATCH + 1, dtype=np.uint32)
+        pos = np.full(BATCH, PREFILL, np.uint32)
+        out = np.zeros((steps + 3) * BATCH, np.uint32)
+        Q.check(Q.lib.q_b200_decode_batch_loop(C.byref(m.model), C.byref(m.ctx), Q.ptr(toks), Q.ptr(pos), 3,
+                                               Q.ptr(out), 1), "batch_loop")
+        stream = torch.cuda.ExternalStream(m.stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        pos += 3
+        e0.record(stream)
+        Q.check(Q.lib.q_b200_decode_batch_loop(C.byref(m.model), C.byref(m.ctx), Q.ptr(toks), Q.ptr(pos), steps,
+                                               Q.ptr(out), 0), "batch_loop")
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms[L] = e0.elapsed_time(e1) / steps
+        m.close()
+    layer_ms = (ms[4] - ms[2]) / 2
+    c = dict(CFG70B, layers=1)
+    ctx = PREFILL + 3 + steps // 2
+    layer_bytes = q4_linear_bytes(c) + BATCH * CFG70B["kv_heads"] * ctx * (CFG70B["dim"] // CFG70B["heads"]) * 8
+    head_ms = CFG70B["vocab"] * CFG70B["dim"] * 4 / (peak * 1e9) * 1e3
+    step_ms = CFG70B["layers"] * layer_ms + head_ms
+    return {"batch": BATCH, "context": ctx, "steps": steps,
+            "step_ms_2layer": round(ms[2], 4), "step_ms_4layer": round(ms[4], 4),
+            "layer_us": round(layer_ms * 1e3, 2), "layer_bytes": layer_bytes,
+            "layer_gbs": round(layer_bytes / (layer_ms * 1e-3) / 1e9, 1),
+            "layer_frac": round(layer_bytes / (layer_ms * 1e-3) / 1e9 / peak, 4),
+            "est_tok_s_80_layers": round(BATCH / (step_ms * 1e-3), 1),
+            "source": "q_b200_decode_batch_loop, 70B layer shapes, 2- and 4-layer models (vocab 4096); "
+                      "80-layer figure = 80 x measured layer + LM head at the measured HBM peak (estimate)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -326,10 +385,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--only", choices=["gemv", "attention", "head", "prefill"],
+    ap.add_argument("--no-batch", action="store_true")
+    ap.add_argument("--only", choices=["gemv", "attention", "head", "prefill", "batch"],
                     help="profiling runs: the gate/up GEMV alone, a few decode steps of a "
                          "2-layer 8B-shaped model (small vocab) over a 2048-position cache, "
-                         "or the FP32 LM-head GEMV (128256 x 4096) alone")
+                         "the FP32 LM-head GEMV (128256 x 4096) alone, a 2048-row prompt through "
+                         "2 8B-shaped layers, or the batch-16 decode of 70B-shaped layers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -403,6 +464,10 @@ def main():
         for _ in range(max(1, args.steps)):
             ms.forward(toks, 0)
         print(json.dumps({"only": "prefill", "calls": max(1, args.steps)}), flush=True)
+        return
+    if args.only == "batch":
+        import qorus_b200 as Q
+        print(json.dumps({"only": "batch", **batch_measure(Q, torch, 6450.9, max(4, args.steps))}), flush=True)
         return
     if args.only == "attention":
         import qorus_b200 as Q
@@ -529,6 +594,9 @@ def main():
     prefill = None
     if world == 1 and not args.no_prefill:
         prefill = prefill_measure(Q, m, torch, float(peaks.get("bf16_tflops", 1590.0)))
+    batch = None
+    if world == 1 and not args.no_batch:
+        batch = batch_measure(Q, torch, peak)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -564,6 +632,7 @@ def main():
             "cpu_baseline": cpu,
             "sweep": sweep,
             "prefill": prefill,
+            "batch_decode": batch,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 16,
                     "d2h_bytes_per_step": CFG8B["vocab"] * 4},
             "gpu_launches": int(launches),

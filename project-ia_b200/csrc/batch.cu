@@ -38,7 +38,9 @@ static cudaError_t launch_xprep(DevState* s, const BatchPrepArgs& a, cudaStream_
     if (e != cudaSuccess) return e;
     if ((size_t)a.K * 4 > 220 * 1024) return cudaErrorInvalidValue;
     (void)s;
-    return launch_ex(batch_xprep_kernel, dim3(a.TG * 8), dim3(256), (size_t)a.K * 4, st, true, a);
+    // slices: enough CTAs that the conversion is not left to 8-16 SMs
+    const uint32_t slices = std::max<uint32_t>(1, std::min<uint32_t>(a.K / 256, 128 / (a.TG * 8)));
+    return launch_ex(batch_xprep_kernel, dim3(a.TG * 8, slices), dim3(256), (size_t)a.K * 4, st, true, a);
 }
 
 static cudaError_t launch_bgemv(DevState* s, const uint8_t* w, const GemvPlan& p, BatchGemvArgs a, cudaStream_t st) {

@@ -31,7 +31,7 @@
 namespace qb200 {
 
 static constexpr uint32_t BT_MAXB = 16;    // sequences per batch
-static constexpr int BT_WARPS = 8;         // consumer warps
+static constexpr int BT_WARPS = 8;         // consumer warps (12 and 16 measured no faster)
 static constexpr int BT_THREADS = BT_WARPS * 32 + 32;
 static constexpr uint32_t BT_NS = 4;       // slabs streamed together
 static constexpr uint32_t BT_SB = 16;      // blocks per ring stage
@@ -66,13 +66,19 @@ __device__ __forceinline__ int bt_exponent(float maxabs) {
     return min(max(15 - E, -100), 100);
 }
 
-// One CTA per input row (TG * 8 CTAs; rows >= B write zeros).
+// Grid (TG * 8 input rows, slices): every CTA of a row reads the whole row
+// (its sum of squares and maximum are row-wide) and writes the fragments of
+// its slice of the blocks; rows >= B write zeros.  The trigger comes first:
+// the GEMV after it streams its weights meanwhile and waits for the whole
+// grid before it reads a fragment.
 __global__ void __launch_bounds__(256) batch_xprep_kernel(const BatchPrepArgs a) {
     extern __shared__ __align__(16) float brow[];
     __shared__ float s_red[8];
     __shared__ uint32_t s_max;
     const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t K = a.K, nb = K / 32;
+    const uint32_t q0 = nb * 8 * blockIdx.y / gridDim.y, q1 = nb * 8 * (blockIdx.y + 1) / gridDim.y;
+    pdl_trigger();
     pdl_wait();
     if (tid == 0) s_max = 0u;
     const bool live = b < a.B;
@@ -82,7 +88,7 @@ __global__ void __launch_bounds__(256) batch_xprep_kernel(const BatchPrepArgs a)
         for (uint32_t i = tid; i < K / 4; i += 256) {
             const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
             reinterpret_cast<float4*>(brow)[i] = v;
-            if (a.x_copy) reinterpret_cast<float4*>(a.x_copy + (size_t)b * K)[i] = v;
+            if (a.x_copy && blockIdx.y == 0) reinterpret_cast<float4*>(a.x_copy + (size_t)b * K)[i] = v;
             ss = __fmaf_rn(v.x, v.x, ss);
             ss = __fmaf_rn(v.y, v.y, ss);
             ss = __fmaf_rn(v.z, v.z, ss);
@@ -115,10 +121,10 @@ __global__ void __launch_bounds__(256) batch_xprep_kernel(const BatchPrepArgs a)
     __syncthreads();
     const int e = bt_exponent(__uint_as_float(s_max));
     const float mul = ldexpf(1.0f, e);
-    if (tid == 0 && live) a.tscale[b] = ldexpf(1.0f, -e);
+    if (tid == 0 && live && blockIdx.y == 0) a.tscale[b] = ldexpf(1.0f, -e);
     const uint32_t tg = b >> 3, g = b & 7;
     // thread: four consecutive k of one (block, step, t)
-    for (uint32_t q = tid; q < nb * 8; q += 256) {
+    for (uint32_t q = q0 + tid; q < q1; q += 256) {
         const uint32_t blk = q >> 3, st = (q >> 2) & 1, t = q & 3;
         const uint32_t k = blk * 32 + st * 16 + 4 * t;
         uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
@@ -137,7 +143,6 @@ __global__ void __launch_bounds__(256) batch_xprep_kernel(const BatchPrepArgs a)
         uint32_t* dst = a.frag + (((size_t)blk * a.TG + tg) * 32 + g * 4 + t) * BT_FRAG_WORDS + st * 4;
         *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], lw[0], lw[1]);
     }
-    pdl_trigger();
 }
 
 // ---- the batched GEMV ---------------------------------------------------------------
@@ -272,8 +277,22 @@ __global__ void __launch_bounds__(BT_THREADS, 1) q4_batch_kernel(const BatchGemv
     pdl_wait();
     const uint32_t g = lane >> 2, t = lane & 3;
     uint32_t s = 0, ph = 0;
+    // input fragments of block blk: [TG][lane][8 words]; a warp takes blocks
+    // warp, warp + NW, ... (BT_SB is a multiple of NW), so the next block's
+    // fragments are loaded (from L2) while this one's MMAs run
+    auto load_frag = [&](uint4 (&xf)[TG][2], uint32_t blk) {
+#pragma unroll
+        for (int q = 0; q < TG; ++q) {
+            const uint4* src = reinterpret_cast<const uint4*>(a.frag + (((size_t)blk * a.TG + q) * 32 + lane) * BT_FRAG_WORDS);
+            xf[q][0] = __ldcg(src);
+            xf[q][1] = __ldcg(src + 1);
+        }
+    };
+    static_assert(BT_SB % BT_WARPS == 0, "a warp's blocks follow one another across stages");
     for (uint32_t jp = j0; jp < j1; jp += BT_NS) {
         const uint32_t ns = min(BT_NS, j1 - jp);
+        uint4 nxt[TG][2];
+        if (warp < nb) load_frag(nxt, warp);
         float acc[BT_NS][2][TG][4];
 #pragma unroll
         for (int i = 0; i < (int)BT_NS; ++i)
@@ -288,15 +307,13 @@ __global__ void __launch_bounds__(BT_THREADS, 1) q4_batch_kernel(const BatchGemv
             const uint32_t b0 = bs * BT_SB, n = min(BT_SB, nb - b0);
             for (uint32_t bi = warp; bi < n; bi += NW) {
                 const uint32_t blk = b0 + bi;
-                // input fragments of this block: [TG][lane][8 words]
                 uint4 xf[TG][2];
 #pragma unroll
                 for (int q = 0; q < TG; ++q) {
-                    const uint4* src =
-                        reinterpret_cast<const uint4*>(a.frag + (((size_t)blk * a.TG + q) * 32 + lane) * BT_FRAG_WORDS);
-                    xf[q][0] = __ldcg(src);
-                    xf[q][1] = __ldcg(src + 1);
+                    xf[q][0] = nxt[q][0];
+                    xf[q][1] = nxt[q][1];
                 }
+                if (blk + NW < nb) load_frag(nxt, blk + NW);
 #pragma unroll
                 for (int i = 0; i < (int)BT_NS; ++i) {
                     if ((uint32_t)i >= ns) break;
