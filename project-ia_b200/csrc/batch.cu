@@ -111,20 +111,20 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
         aa.n_heads = t.nh;
         aa.n_kv_heads = t.nkv;
         aa.max_seq = c.max_seq_len;
-        aa.chunk_alloc = s->att_ca;
-        aa.slots = s->att_slots;
+        aa.chunk_alloc = b.att_ca;
+        aa.slots = b.att_slots;
         aa.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
         aa.seq_stride = t.d;
         aa.n_layers = L;
         {
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(s->att_cs, t.nkv, b.B);
+            cfg.gridDim = dim3(b.att_cs, t.nkv, b.B);
             cfg.blockDim = dim3(ATT_THREADS);
-            cfg.dynamicSmemBytes = s->att_smem;
+            cfg.dynamicSmemBytes = b.att_smem;
             cfg.stream = st;
             cudaLaunchAttribute attr[2];
             attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = s->att_cs;
+            attr[0].val.clusterDim.x = b.att_cs;
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
             attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -206,6 +206,33 @@ q_error_code batch_init(DevState* s, uint32_t B) {
         return Q_ERR_ALLOC_FAILED;
     }
     Q_CUDA(cudaMemset(b.kv, 0, kv_seq * B));
+    {
+        // the smallest cluster (2..16) that still gives every SM a CTA: at
+        // 70B shapes and B = 16 that is 2 (measured per 70B layer: 345-381 us
+        // at 2, 392 at 4, 401 at 8, 464 at 16, 368 at 1)
+        uint32_t cs = 2;
+        while (cs < 16 && (size_t)B * t.nkv * cs < (size_t)device_sms()) cs *= 2;
+        const uint32_t G = c.n_heads / c.n_kv_heads;
+        const uint32_t sp = ATT_STAGE_BYTES / (s->hd * 4);
+        const uint32_t ca = ((c.max_seq_len + sp - 1) / sp + cs - 1) / cs * sp;
+        const size_t limit = 227 * 1024 - 8 * 1024;
+        b.att_slots = 0;
+        for (uint32_t slots = ATT_MAX_SLOTS; slots >= 2 && !b.att_slots; --slots)
+            if (attn_smem_bytes(G, s->hd, ca, slots) <= limit) {
+                b.att_slots = slots;
+                b.att_smem = attn_smem_bytes(G, s->hd, ca, slots);
+            }
+        if (!b.att_slots) {
+            free_batch(s);
+            return Q_ERR_INVALID_CONFIG;
+        }
+        b.att_cs = cs;
+        b.att_ca = ca;
+        const void* kern = attn_kernel_for(s->hd, G);
+        if (cs > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        Q_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)std::max(b.att_smem, s->att_smem)));
+    }
     const size_t sz[] = {bal(B * D * 4), bal(B * (size_t)t.d * 4), bal(B * (size_t)t.d * 4), bal(B * (size_t)t.h * 4),
                          bal(B * V * 4), bal(Kmax / 32 * b.TG * 32 * BT_FRAG_WORDS * 4), bal(BT_MAXB * 4),
                          bal(BT_MAXB * sizeof(StepParams)), bal(BT_MAXB * 8), bal((size_t)b.tok_cap * B * 4), bal(4),

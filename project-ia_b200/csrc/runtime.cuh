@@ -127,6 +127,10 @@ struct BatchState {
     uint32_t tok_cap = 0;
     StepParams* h_step = nullptr;  // pinned [B]
     float wmul = 1.0f, wdiv = 1.0f;  // LM head scale
+    // attention launch shape of the batch: with B * n_kv clusters there is
+    // parallelism enough for fewer, longer chunks per sequence
+    uint32_t att_cs = 0, att_ca = 0, att_slots = 0;
+    size_t att_smem = 0;
     cudaGraphExec_t graph = nullptr;
     uint64_t kernels = 0;
 };
