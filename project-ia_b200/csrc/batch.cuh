@@ -427,29 +427,40 @@ __global__ void __launch_bounds__(256) batch_head_kernel(const BatchHeadArgs a) 
         float acc[TG][4];
 #pragma unroll
         for (int q = 0; q < TG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.0f;
-        // W of block blk + 1 is requested while block blk is multiplied
-        float4 cur[2][2], nxt[2][2];
+        // W of blocks blk + 1 and blk + 2 are in flight while block blk is
+        // multiplied (two blocks ahead: a warp walks its rows block by block,
+        // so the loads in flight per warp set the bandwidth)
+        float4 cur[2][2], nxt[2][2], nx2[2][2];
+        auto load_w = [&](float4 (&dst)[2][2], uint32_t blk) {
 #pragma unroll
-        for (int st = 0; st < 2; ++st) {
-            cur[st][0] = ldg_stream_f4(reinterpret_cast<const float4*>(wa + st * 16 + 4 * t));
-            cur[st][1] = ldg_stream_f4(reinterpret_cast<const float4*>(wb + st * 16 + 4 * t));
-        }
-        for (uint32_t blk = 0; blk < nb; ++blk) {
-            if (blk + 1 < nb) {
-#pragma unroll
-                for (int st = 0; st < 2; ++st) {
-                    const uint32_t k = (blk + 1) * 32 + st * 16 + 4 * t;
-                    nxt[st][0] = ldg_stream_f4(reinterpret_cast<const float4*>(wa + k));
-                    nxt[st][1] = ldg_stream_f4(reinterpret_cast<const float4*>(wb + k));
-                }
+            for (int st = 0; st < 2; ++st) {
+                const uint32_t k = blk * 32 + st * 16 + 4 * t;
+                dst[st][0] = ldg_stream_f4(reinterpret_cast<const float4*>(wa + k));
+                dst[st][1] = ldg_stream_f4(reinterpret_cast<const float4*>(wb + k));
             }
-            uint4 xf[TG][2];
+        };
+        // the inputs' fragments of block blk + 1 are requested with them
+        auto load_x = [&](uint4 (&dst)[TG][2], uint32_t blk) {
 #pragma unroll
             for (int q = 0; q < TG; ++q) {
                 const uint4* src = reinterpret_cast<const uint4*>(a.frag + (((size_t)blk * a.TG + q) * 32 + lane) * BT_FRAG_WORDS);
-                xf[q][0] = __ldcg(src);
-                xf[q][1] = __ldcg(src + 1);
+                dst[q][0] = __ldcg(src);
+                dst[q][1] = __ldcg(src + 1);
             }
+        };
+        uint4 xnext[TG][2];
+        load_w(cur, 0);
+        if (nb > 1) load_w(nxt, 1);
+        load_x(xnext, 0);
+        for (uint32_t blk = 0; blk < nb; ++blk) {
+            if (blk + 2 < nb) load_w(nx2, blk + 2);
+            uint4 xf[TG][2];
+#pragma unroll
+            for (int q = 0; q < TG; ++q) {
+                xf[q][0] = xnext[q][0];
+                xf[q][1] = xnext[q][1];
+            }
+            if (blk + 1 < nb) load_x(xnext, blk + 1);
             float d[TG][4];
 #pragma unroll
             for (int q = 0; q < TG; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.0f;
@@ -483,6 +494,8 @@ __global__ void __launch_bounds__(256) batch_head_kernel(const BatchHeadArgs a) 
             for (int st = 0; st < 2; ++st) {
                 cur[st][0] = nxt[st][0];
                 cur[st][1] = nxt[st][1];
+                nxt[st][0] = nx2[st][0];
+                nxt[st][1] = nx2[st][1];
             }
         }
         // D: rows g (e < 2) / g + 8, inputs 8 q + 2 t + (e & 1)
