@@ -98,8 +98,11 @@ const float* q_b200_device_logits(q_context* ctx);
  * src/main.c:994-1131).  These calls decode up to 16 sequences together,
  * every weight streamed from HBM once per step for all of them.  Sequence b
  * has its own KV cache in the upstream layout [L][n_kv][max_seq][K|V]
- * (allocated by q_b200_batch_init, beside ctx's single-sequence cache).
- * Single-GPU contexts, after llama_build_graph. */
+ * (allocated by q_b200_batch_init, beside ctx's single-sequence cache),
+ * after llama_build_graph.  On a tensor-parallel context every rank makes
+ * the same calls (they are collective), each cache holds the rank's KV
+ * heads, the partial residuals and argmax keys are all-reduced with NCCL,
+ * and q_b200_decode_batch returns every rank the full [B][vocab] logits. */
 
 /* Allocate the B caches (zeroed) and step state, capture the batched step. */
 q_error_code q_b200_batch_init(q_context* ctx, q_llama_model* model, uint32_t batch);

@@ -21,6 +21,7 @@ void free_batch(DevState* s) {
     if (b.graph) cudaGraphExecDestroy(b.graph);
     if (b.base) cudaFree(b.base);
     if (b.kv) cudaFree(b.kv);
+    if (b.gath) cudaFree(b.gath);
     if (b.h_step) cudaFreeHost(b.h_step);
     b = BatchState{};
 }
@@ -61,6 +62,17 @@ static cudaError_t launch_bgemv(DevState* s, const uint8_t* w, const GemvPlan& p
     const uint32_t grid = std::min<uint32_t>(p.n_slabs, (uint32_t)device_sms());
     if (b.TG == 1) return launch_ex(q4_batch_kernel<1>, dim3(grid), dim3(BT_THREADS), BT_SMEM, st, true, a);
     return launch_ex(q4_batch_kernel<2>, dim3(grid), dim3(BT_THREADS), BT_SMEM, st, true, a);
+}
+
+// Tensor parallelism: in-place NCCL all-reduce of a batch buffer (the B
+// partial residual updates of wo / down, B * dim floats; or the B argmax
+// keys with max).  A no-op on one GPU.
+static cudaError_t batch_allreduce(DevState* s, void* buf, size_t count, bool keys, cudaStream_t st) {
+    if (s->tp_world == 1) return cudaSuccess;
+    const NcclApi* n = nccl();
+    if (!n || !s->comm) return cudaErrorUnknown;
+    return nccl_status(keys ? n->all_reduce(buf, buf, count, ncclUint64, ncclMax, s->comm, st)
+                            : n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, s->comm, st));
 }
 
 static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
@@ -139,11 +151,12 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
         }
         if ((e = prep(b.att, t.d, t.d, nullptr, false, nullptr)) != cudaSuccess) break;
         g = BatchGemvArgs{};
-        g.epi = EPI_RESID;
+        g.epi = residual_epi(s);  // tensor parallel: rank 0 adds the residual, the others their partial
         g.y = b.x;
         g.resid = b.x;
         g.ldy = D;
         if ((e = launch_bgemv(s, s->wo[l], s->p_wo, g, st)) != cudaSuccess) break;
+        if ((e = batch_allreduce(s, b.x, (size_t)b.B * D, false, st)) != cudaSuccess) break;
         if ((e = prep(b.x, D, D, s->ffn_norm + (size_t)l * D, false, nullptr)) != cudaSuccess) break;
         g = BatchGemvArgs{};
         g.epi = EPI_SILU;
@@ -152,17 +165,20 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
         if ((e = launch_bgemv(s, s->gu[l], s->p_gu, g, st)) != cudaSuccess) break;
         if ((e = prep(b.h, H, H, nullptr, false, nullptr)) != cudaSuccess) break;
         g = BatchGemvArgs{};
-        g.epi = EPI_RESID;
+        g.epi = residual_epi(s);
         g.y = b.x;
         g.resid = b.x;
         g.ldy = D;
         if ((e = launch_bgemv(s, s->down[l], s->p_down, g, st)) != cudaSuccess) break;
+        if ((e = batch_allreduce(s, b.x, (size_t)b.B * D, false, st)) != cudaSuccess) break;
     }
     if (e != cudaSuccess) return e;
     if ((e = prep(b.x, D, D, s->out_norm, false, nullptr)) != cudaSuccess) return e;
     BatchHeadArgs h{};
     h.w = s->out_w;
-    h.V = c.vocab_size;
+    h.V = t.v;
+    h.row_base = t.v0;
+    h.ldl = s->tp_world > 1 ? t.v_pad : t.v;
     h.K = D;
     h.B = b.B;
     h.TG = b.TG;
@@ -176,6 +192,7 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
     e = b.TG == 1 ? launch_ex(batch_head_kernel<1>, hg, dim3(256), 0, st, true, h)
                   : launch_ex(batch_head_kernel<2>, hg, dim3(256), 0, st, true, h);
     if (e != cudaSuccess) return e;
+    if ((e = batch_allreduce(s, b.best, b.B, true, st)) != cudaSuccess) return e;
     BatchAdvanceArgs ad{};
     ad.step = b.step;
     ad.best = b.best;
@@ -187,7 +204,7 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
 }
 
 q_error_code batch_init(DevState* s, uint32_t B) {
-    if (!s->built || s->tp_world != 1) return Q_ERR_INVALID_ARG;
+    if (!s->built || (s->tp_world > 1 && !s->comm)) return Q_ERR_INVALID_ARG;
     if (B == 0 || B > BT_MAXB) return Q_ERR_INVALID_SIZE;
     const q_llama_config& c = s->cfg;
     const TpShape& t = s->tp;
@@ -206,6 +223,11 @@ q_error_code batch_init(DevState* s, uint32_t B) {
         return Q_ERR_ALLOC_FAILED;
     }
     Q_CUDA(cudaMemset(b.kv, 0, kv_seq * B));
+    if (s->tp_world > 1 &&
+        !cuda_ok(dev_malloc(&b.gath, (size_t)s->tp_world * B * t.v_pad * 4), "dev_malloc(batch logits gather)")) {
+        free_batch(s);
+        return Q_ERR_ALLOC_FAILED;
+    }
     {
         // the smallest cluster (2..16) that still gives every SM a CTA: at
         // 70B shapes and B = 16 that is 2 (measured per 70B layer: 345-381 us
@@ -400,9 +422,28 @@ q_error_code q_b200_decode_batch(q_llama_model* model, q_context* ctx, const uin
     q_error_code rc = q_b200_decode_batch_loop(model, ctx, tokens, pos, 1, next_tokens, 1);
     if (rc != Q_OK) return rc;
     DevState* s = state_of(ctx, false);
-    if (logits)
-        Q_CUDA(cudaMemcpy(logits, s->batch.logits, (size_t)s->batch.B * model->config.vocab_size * 4,
-                          cudaMemcpyDeviceToHost));
+    if (!logits) return Q_OK;
+    const BatchState& b = s->batch;
+    const uint32_t V = model->config.vocab_size;
+    if (s->tp_world == 1) {
+        Q_CUDA(cudaMemcpy(logits, b.logits, (size_t)b.B * V * 4, cudaMemcpyDeviceToHost));
+        return Q_OK;
+    }
+    // every rank's [B][v_pad] rows, gathered in rank order (a collective: all
+    // ranks call this together, as they do llama_forward), then reordered
+    const NcclApi* n = nccl();
+    if (!n || !s->comm) return Q_ERR_INVALID_ARG;
+    const size_t per = (size_t)b.B * s->tp.v_pad;
+    Q_CUDA(nccl_status(n->all_gather(b.logits, b.gath, per, ncclFloat32, s->comm, s->stream)));
+    std::vector<float> all(per * s->tp_world);
+    Q_CUDA(cudaMemcpyAsync(all.data(), b.gath, all.size() * 4, cudaMemcpyDeviceToHost, s->stream));
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    for (uint32_t r = 0; r < s->tp_world; ++r) {
+        const uint32_t v0 = std::min(V, r * s->tp.v_pad), v1 = std::min(V, v0 + s->tp.v_pad);
+        for (uint32_t q = 0; q < b.B; ++q)
+            std::memcpy(logits + (size_t)q * V + v0, all.data() + r * per + (size_t)q * s->tp.v_pad,
+                        (size_t)(v1 - v0) * 4);
+    }
     return Q_OK;
 }
 

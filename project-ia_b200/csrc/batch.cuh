@@ -396,12 +396,14 @@ __global__ void __launch_bounds__(BT_THREADS, 1) q4_batch_kernel(const BatchGemv
 // hi + lo fragments (the three products hi*hi, hi*lo, lo*hi per K step,
 // every product exact, fp32 accumulation promoted into registers every 32 K).
 struct BatchHeadArgs {
-    const float* w;          // [V][K]
+    const float* w;          // [V][K]: this rank's vocabulary rows under tensor parallelism
     uint32_t V, K, B, TG;
+    uint32_t row_base;       // global index of row 0 (vocabulary split)
+    uint32_t ldl;            // logits row stride (>= V)
     float wmul, wdiv;        // 2^wexp, 2^-wexp
     const uint32_t* frag;    // normalized inputs, batch_xprep_kernel layout
     const float* tscale;     // [B]
-    float* logits;           // [B][V]
+    float* logits;           // [B][ldl]
     unsigned long long* best;  // [B] argmax keys
 };
 
@@ -506,11 +508,11 @@ __global__ void __launch_bounds__(256) batch_head_kernel(const BatchHeadArgs a) 
                 const uint32_t b = 8 * q + 2 * t + (e & 1), row = e < 2 ? ra : rb;
                 if (b >= a.B || row >= a.V) continue;
                 const float v = acc[q][e] * a.wdiv * __ldg(a.tscale + b);
-                a.logits[(size_t)b * a.V + row] = v;
+                a.logits[(size_t)b * a.ldl + row] = v;
                 // order-preserving key, lowest index wins ties (upstream main.c:870-881)
                 const uint32_t u = __float_as_uint(v);
                 const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-                atomicMax(&s_best[b], ((unsigned long long)ord << 32) | (0xFFFFFFFFu - row));
+                atomicMax(&s_best[b], ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (a.row_base + row)));
             }
     }
     __syncthreads();

@@ -121,6 +121,7 @@ struct BatchState {
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
     uint32_t* frag = nullptr;      // input fragments of the next GEMV
     float* tscale = nullptr;
+    float* gath = nullptr;         // tensor parallel: [world][B][v_pad] gathered logits
     StepParams* step = nullptr;    // [B]
     unsigned long long* best = nullptr;
     uint32_t *tok_out = nullptr, *tok_count = nullptr;

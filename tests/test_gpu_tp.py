@@ -179,3 +179,97 @@ def test_tp_wide_matches_oracle(tmp_path, world, fused):
         err = np.abs(lg[:, : WIDE["vocab"]] - np.stack(ref)).max()
         assert err <= LOGIT_TOL, f"rank {rank}: logits max-abs {err:.3e}"
         assert loop == solo_loop, (rank, loop, solo_loop)
+
+
+# ---- batched decode on 2, 4 and 8 ranks ---------------------------------------
+
+def _batch_run(m, cfg, kvs, toks, pos, rank=0, world=1):
+    import ctypes as C
+    B = len(kvs)
+    Q.check(Q.lib.q_b200_batch_init(C.byref(m.ctx), C.byref(m.model), B), "batch_init")
+    hd = cfg.dim // cfg.n_heads
+    for b, kv in enumerate(kvs):
+        if world > 1:
+            sh = Q.tp_shape(cfg, rank, world)
+            h0 = sh["kv0"] // hd
+            kv = np.ascontiguousarray(kv.reshape(cfg.n_layers, cfg.n_kv_heads, -1)[:, h0: h0 + sh["nkv"]]).ravel()
+        Q.check(Q.lib.q_b200_batch_kv_write(C.byref(m.ctx), b, 0, Q.ptr(kv), kv.nbytes), "batch_kv_write")
+    V = cfg.vocab_size
+    logits = np.zeros(B * V, np.float32)
+    nxt = np.zeros(B, np.uint32)
+    Q.check(Q.lib.q_b200_decode_batch(C.byref(m.model), C.byref(m.ctx), Q.ptr(toks), Q.ptr(pos), Q.ptr(logits),
+                                      Q.ptr(nxt)), "decode_batch")
+    out = np.zeros(6 * B, np.uint32)
+    pos1 = (pos + 1).astype(np.uint32)
+    Q.check(Q.lib.q_b200_decode_batch_loop(C.byref(m.model), C.byref(m.ctx), Q.ptr(nxt), Q.ptr(pos1), 6,
+                                           Q.ptr(out), 1), "decode_batch_loop")
+    return logits.reshape(B, V), nxt, out.reshape(6, B)
+
+
+def _batch_worker(rank, world, port, path, kvs, toks, pos, out):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        box = [Q.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+
+        def gather(b):
+            allb = [None] * world
+            dist.all_gather_object(allb, b)
+            return allb
+        m = Q.Model(path, tp=(rank, world, box[0]), tp_gather=gather)
+        out.put((rank, *_batch_run(m, Q.config(**WIDE), kvs, toks, pos, rank, world)))
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_batched_decode_matches_single_gpu(tmp_path, world):
+    """Five sequences with ragged pre-filled caches decoded together on
+    `world` ranks (partial residuals and argmax keys all-reduced, vocabulary
+    rows gathered): one step's logits of every sequence equal one GPU's
+    batched step (max-abs <= 1e-2), and the next 6 device-fed tokens of every
+    sequence are the same."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import ctypes as C
+    import torch.multiprocessing as mp
+    cfg = Q.config(**WIDE)
+    path = str(tmp_path / "wide.qorus")
+    Q.write_model(path, cfg, seed=7, threads=8)
+    lens = [17, 60, 3, 111, 200]
+    n = cfg.n_layers * cfg.n_kv_heads * cfg.max_seq_len * 2 * (cfg.dim // cfg.n_heads)
+    kvs = []
+    for b, ln in enumerate(lens):
+        kv = np.zeros(n, np.float32)
+        assert Q.lib.q_b200_fill_kv_prefill(Q.ptr(kv), C.byref(cfg), ln, 40 + b, 0) == 0
+        kvs.append(kv)
+    toks = np.array([5, 99, 700, 3, 256], np.uint32)
+    pos = np.array(lens, np.uint32)
+    solo = Q.Model(path)
+    ref_logits, ref_next, ref_loop = _batch_run(solo, cfg, kvs, toks, pos)
+    solo.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batch_worker, args=(r, world, port, path, kvs, toks, pos, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r = q.get(timeout=300)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank in range(world):
+        _, lg, nxt, loop = res[rank]
+        err = np.abs(lg - ref_logits).max()
+        assert err <= LOGIT_TOL, f"rank {rank}: logits max-abs {err:.3e}"
+        assert list(nxt) == list(ref_next)
+        assert (loop == ref_loop).all(), (rank, loop, ref_loop)
