@@ -168,11 +168,12 @@ static q_error_code ready(q_llama_model* model, q_context* ctx, DevState** out) 
     return Q_OK;
 }
 
-// Prompts of more than one row on a single-GPU context take the tensor-core
-// prefill path (csrc/prefill.cu); QORUS_B200_PREFILL=0 forces the row replay
-// below, as do tensor-parallel contexts.
+// Prompts of more than one row take the tensor-core prefill path
+// (csrc/prefill.cu; on tensor-parallel contexts every rank runs its shard and
+// the partial residuals are all-reduced); QORUS_B200_PREFILL=0 forces the
+// row replay below.
 static bool use_prefill(const DevState* s, uint32_t seq_len) {
-    if (seq_len < 2 || s->tp_world != 1) return false;
+    if (seq_len < 2) return false;
     const char* e = std::getenv("QORUS_B200_PREFILL");
     return !(e && e[0] == '0');
 }

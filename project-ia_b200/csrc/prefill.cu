@@ -170,10 +170,19 @@ static cudaError_t launch_pf_attention(DevState* s, float* kv, uint32_t layer, u
     return cudaLaunchKernel(kern, grid, dim3(tc ? PT_THREADS : PF_ATT_THREADS), params, smem, st);
 }
 
+// Tensor parallelism: in-place sum of the S x dim partial residuals over the
+// ranks (NCCL; 32 MB at 2048 rows of the 8B shape).  A no-op on one GPU.
+static cudaError_t pf_allreduce(DevState* s, float* buf, size_t count, cudaStream_t st) {
+    if (s->tp_world == 1) return cudaSuccess;
+    const NcclApi* n = nccl();
+    if (!n || !s->comm) return cudaErrorUnknown;
+    return nccl_status(n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, s->comm, st));
+}
+
 q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t S, uint32_t pos, bool sample) {
     const q_llama_config& c = s->cfg;
     const TpShape& t = s->tp;
-    if (s->tp_world != 1) return Q_ERR_INVALID_ARG;
+    if (s->tp_world != 1 && (sample || !s->comm)) return Q_ERR_INVALID_ARG;
     q_error_code rc = prefill_workspace(s, S);
     if (rc != Q_OK) return rc;
     cudaStream_t st = s->stream;
@@ -222,11 +231,12 @@ q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_
         Q_CUDA(launch_act_split(s, as, S, st));
         Q_CUDA(launch_w_split(s, s->wo[l], s->p_wo, st));
         g = PfGemmArgs{};
-        g.epi = EPI_RESID;
+        g.epi = residual_epi(s);  // tensor parallel: rank 0 adds the residual, the others their partial
         g.y = s->pf_x;
         g.resid = s->pf_x;
         g.ldy = D;
         Q_CUDA(launch_pf_gemm(s, S, D, t.d, g, st));
+        Q_CUDA(pf_allreduce(s, s->pf_x, (size_t)S * D, st));
         // feed-forward block
         as = ActSplitArgs{};
         as.x = s->pf_x;
@@ -254,11 +264,12 @@ q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_
         Q_CUDA(launch_act_split(s, as, S, st));
         Q_CUDA(launch_w_split(s, s->down[l], s->p_down, st));
         g = PfGemmArgs{};
-        g.epi = EPI_RESID;
+        g.epi = residual_epi(s);
         g.y = s->pf_x;
         g.resid = s->pf_x;
         g.ldy = D;
         Q_CUDA(launch_pf_gemm(s, S, D, H, g, st));
+        Q_CUDA(pf_allreduce(s, s->pf_x, (size_t)S * D, st));
     }
     // last row: LM head + argmax, then the step advance (the next decode
     // step then runs at pos + S with the argmax as its token)
