@@ -331,7 +331,6 @@ q_error_code q_generate(q_generation_state* st) {
     // thread's xorshift state, carried to the device and back
     const bool sample = st->temperature >= 1e-6f;
     if (sample) {
-        if (s->tp_world != 1) return Q_ERR_INVALID_ARG;  // sampling needs one rank's whole vocabulary
         if ((rc = ensure_sample_graph(st->ctx, s)) != Q_OK) return rc;
         const SampleParams prm{st->temperature, st->top_k, st->top_p, 0u};
         Q_CUDA(cudaMemcpy(s->samp, &prm, sizeof prm, cudaMemcpyHostToDevice));

@@ -536,7 +536,7 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
     const bool fused = tp_fused(s);
     if (fused) {  // argmax keys over peer memory; the receive of the last down exchange if asked
         tp_geometry(s, h.tp);
-        h.tp_key = 1;
+        h.tp_key = sample ? 0u : 1u;  // a sampled token comes from the gathered logits instead
         if (tp_recv) {
             h.tp.tp_recv = 1;
             h.tp.tp_par = 1;
@@ -576,9 +576,21 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
         if (e != cudaSuccess) return e;
     }
     if (sample) {
-        if (s->tp_world != 1) return cudaErrorInvalidValue;  // the sampler needs the whole vocabulary
+        // the sampler needs the whole vocabulary: on a tensor-parallel
+        // context every rank gathers all ranks' rows (rank order = vocabulary
+        // order) and draws the same token from the same random state
+        if (s->tp_world > 1) {
+            if (s->peers_ready) {
+                e = tp_allreduce(s, s->logits, s->tp.v_pad, TP_GATHER_F32, st, s->logits_all);
+            } else {
+                const NcclApi* n = nccl();
+                if (!n) return cudaErrorUnknown;
+                e = nccl_status(n->all_gather(s->logits, s->logits_all, s->tp.v_pad, ncclFloat32, s->comm, st));
+            }
+            if (e != cudaSuccess) return e;
+        }
         SampleArgs sa{};
-        sa.logits = s->logits;
+        sa.logits = s->tp_world > 1 ? s->logits_all : s->logits;
         sa.V = s->cfg.vocab_size;
         sa.params = s->samp;
         sa.rng = s->rng;
@@ -596,7 +608,7 @@ static cudaError_t enqueue_head(DevState* s, cudaStream_t st, const float* x = n
     a.token_cap = s->tok_cap;
     a.last_token = s->last_tok;
     a.trace = take_slot(s);
-    if (fused) {
+    if (fused && !sample) {
         a.key_ctl = reinterpret_cast<uint32_t*>(s->peers.base[s->tp_rank] + h.tp.tp_off +
                                                 (size_t)2 * s->tp_world * s->peer_slice * 8);
         a.key_world = s->tp_world;

@@ -182,7 +182,7 @@ static cudaError_t pf_allreduce(DevState* s, float* buf, size_t count, cudaStrea
 q_error_code run_prefill(DevState* s, float* kv, const uint32_t* tokens, uint32_t S, uint32_t pos, bool sample) {
     const q_llama_config& c = s->cfg;
     const TpShape& t = s->tp;
-    if (s->tp_world != 1 && (sample || !s->comm)) return Q_ERR_INVALID_ARG;
+    if (s->tp_world != 1 && !s->comm) return Q_ERR_INVALID_ARG;
     q_error_code rc = prefill_workspace(s, S);
     if (rc != Q_OK) return rc;
     cudaStream_t st = s->stream;

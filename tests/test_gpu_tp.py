@@ -273,3 +273,88 @@ def test_tp_batched_decode_matches_single_gpu(tmp_path, world):
         assert err <= LOGIT_TOL, f"rank {rank}: logits max-abs {err:.3e}"
         assert list(nxt) == list(ref_next)
         assert (loop == ref_loop).all(), (rank, loop, ref_loop)
+
+
+# ---- sampled generation on 2, 4 and 8 ranks -------------------------------------
+
+def _generate_worker(rank, world, port, path, prompt, fused, out):
+    """q_generate with temperature 0.8, top-k 40, top-p 0.9 from a fresh
+    process (the thread's random state starts at upstream's seed)."""
+    import ctypes as C
+    os.environ["QORUS_B200_TP_FUSED"] = "1" if fused else "0"
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    tp = gather = None
+    if world > 1:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        box = [Q.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = (rank, world, box[0])
+
+        def gather(b):
+            allb = [None] * world
+            dist.all_gather_object(allb, b)
+            return allb
+    try:
+        m = Q.Model(path, tp=tp, tp_gather=gather)
+        tok = Q.q_tokenizer()
+        tok.initialized = True
+        tok.eos_token_id = 0xFFFFFFFF
+        n = 20
+        gen = np.zeros(n, np.uint32)
+        st = Q.q_generation_state()
+        st.ctx = C.pointer(m.ctx)
+        st.model = C.pointer(m.model)
+        st.tokenizer = C.pointer(tok)
+        st.prompt_tokens = prompt.ctypes.data_as(C.POINTER(C.c_uint32))
+        st.num_prompt_tokens = len(prompt)
+        st.generated_tokens = gen.ctypes.data_as(C.POINTER(C.c_uint32))
+        st.max_tokens = n
+        st.temperature = 0.8
+        st.top_k = 40
+        st.top_p = 0.9
+        Q.check(Q.lib.q_generate(C.byref(st)), "q_generate")
+        out.put((rank, list(gen[: st.num_generated_tokens])))
+        m.close()
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "kernel"])
+def test_tp_sampled_generate_matches_single_gpu(tmp_path, world, fused):
+    """Temperature / top-k / top-p generation on `world` ranks (logits
+    gathered on every rank, the same draw everywhere) gives the tokens one
+    GPU gives from the same random state."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    cfg = Q.config(**WIDE)
+    path = str(tmp_path / "wide.qorus")
+    Q.write_model(path, cfg, seed=7, threads=8)
+    prompt = np.random.default_rng(5).integers(0, WIDE["vocab"], 24).astype(np.uint32)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p1 = ctx.Process(target=_generate_worker, args=(0, 1, 0, path, prompt, fused, q))
+    p1.start()
+    ref = q.get(timeout=300)[1]
+    p1.join(timeout=120)
+    assert p1.exitcode == 0 and len(ref) == 20
+    port = _free_port()
+    procs = [ctx.Process(target=_generate_worker, args=(r, world, port, path, prompt, fused, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r = q.get(timeout=300)
+        res[r[0]] = r[1]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank in range(world):
+        assert res[rank] == ref, (rank, res[rank], ref)
