@@ -415,8 +415,9 @@ def main():
                        CFG8B["heads"], CFG8B["kv_heads"], max_seq)
         path = ensure_model(O.gen, cfg, max_seq, 0, lambda: None)
         threads = os.cpu_count() or 1
-        warm = 1
+        warm = args.warmup
         kind, times = cpu_reference_decode(path, cfg, warm + args.steps, threads, budget_s=150.0)
+        warm = min(warm, max(1, len(times) - 1))  # the time budget may stop the run early
         times = times[warm:]
         tps = len(times) / sum(times)
         line = {"metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "impl": "reference",
