@@ -107,6 +107,21 @@ const float* q_b200_device_logits(q_context* ctx);
 /* Allocate the B caches (zeroed) and step state, capture the batched step. */
 q_error_code q_b200_batch_init(q_context* ctx, q_llama_model* model, uint32_t batch);
 
+/* The same with paged caches: one pool of n_pages pages, each holding
+ * page_rows consecutive positions (a multiple of 32, or of 128 for head
+ * width 32) of every layer and KV head.  A sequence takes pages as its rows
+ * are written or decoded (each page zeroed when taken), so the pool can be
+ * much smaller than batch * max_seq rows; q_b200_decode_batch(_loop) returns
+ * Q_ERR_ARENA_OOM when it runs out.  q_b200_batch_kv_write/read keep the
+ * upstream byte offsets (whole rows only in this mode; rows without a page
+ * read as zeros). */
+q_error_code q_b200_batch_init_paged(q_context* ctx, q_llama_model* model, uint32_t batch, uint32_t page_rows,
+                                     uint32_t n_pages);
+
+/* Give sequence seq's pages back to the pool (paged caches; a no-op for
+ * contiguous ones): the slot starts empty for its next sequence. */
+q_error_code q_b200_batch_release(q_context* ctx, uint32_t seq);
+
 /* Copy bytes between a host buffer and sequence seq's cache (byte offset
  * into its upstream layout). */
 q_error_code q_b200_batch_kv_write(q_context* ctx, uint32_t seq, size_t offset, const void* host,

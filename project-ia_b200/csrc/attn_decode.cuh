@@ -68,6 +68,10 @@ struct AttnArgs {
     // per sequence, and sequence b's cache planes follow the first b caches
     uint32_t seq_stride;     // floats of q / out per sequence
     uint32_t n_layers;       // planes per sequence = n_layers * n_kv_heads
+    // paged caches (batched decode): sequence b's rows [r * page_rows, (r + 1) * page_rows)
+    // live in page pages[b * pages_per_seq + r]; plane (page * n_layers + layer) * n_kv_heads + head
+    const uint32_t* pages;   // null: contiguous caches
+    uint32_t page_rows, pages_per_seq;
 };
 
 // ring[slots][16 KB] | sc[G][chunk_alloc] | ored[PG][G][hd]
@@ -186,8 +190,14 @@ __global__ void __launch_bounds__(ATT_THREADS, G <= 4 ? 2 : 1)
                 // zeros, are loaded and ignored)
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full[s], ATT_STAGE_BYTES);
-                    tma_load_3d(ring + (size_t)s * ATT_STAGE_BYTES, &kv_map, (int)(pass * HD), (int)sp0,
-                                plane, &full[s], pol);
+                    // a stage never straddles pages (page_rows is a multiple of SP)
+                    int y = (int)sp0, z = plane;
+                    if (a.pages) {
+                        const uint32_t pg = __ldg(a.pages + (size_t)bz * a.pages_per_seq + sp0 / a.page_rows);
+                        y = (int)(sp0 % a.page_rows);
+                        z = (int)(((size_t)pg * a.n_layers + a.layer) * a.n_kv_heads + h);
+                    }
+                    tma_load_3d(ring + (size_t)s * ATT_STAGE_BYTES, &kv_map, (int)(pass * HD), y, z, &full[s], pol);
                 }
                 __syncwarp();
                 if (++s == SL) {

@@ -22,6 +22,7 @@ void free_batch(DevState* s) {
     if (b.base) cudaFree(b.base);
     if (b.kv) cudaFree(b.kv);
     if (b.gath) cudaFree(b.gath);
+    if (b.d_pages) cudaFree(b.d_pages);
     if (b.h_step) cudaFreeHost(b.h_step);
     b = BatchState{};
 }
@@ -107,8 +108,13 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
         g.ldy = t.d;
         g.rope_cos = s->rope_cos;
         g.rope_sin = s->rope_sin;
-        g.kv = b.kv + (size_t)l * layer_floats;
+        g.kv = b.d_pages ? b.kv : b.kv + (size_t)l * layer_floats;
         g.kv_seq_stride = (size_t)L * layer_floats;
+        g.pages = b.d_pages;
+        g.page_rows = b.page_rows;
+        g.pages_per_seq = b.pages_per_seq;
+        g.n_layers = L;
+        g.layer = l;
         g.hd = s->hd;
         g.q_rows = t.d;
         g.kv_rows = t.kvd;
@@ -128,6 +134,9 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
         aa.scale = 1.0f / sqrtf((float)s->hd);  // upstream model.c:1315
         aa.seq_stride = t.d;
         aa.n_layers = L;
+        aa.pages = b.d_pages;
+        aa.page_rows = b.page_rows;
+        aa.pages_per_seq = b.pages_per_seq;
         {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(b.att_cs, t.nkv, b.B);
@@ -203,7 +212,12 @@ static cudaError_t enqueue_batch_step(DevState* s, cudaStream_t st) {
     return launch_ex(batch_advance_kernel, dim3(1), dim3(32), 0, st, true, ad);
 }
 
-q_error_code batch_init(DevState* s, uint32_t B) {
+static constexpr uint32_t kNoPage = 0xFFFFFFFFu;
+
+// page_rows == 0: contiguous caches (one upstream-layout cache per sequence);
+// otherwise a pool of n_pages pages of page_rows rows (a multiple of the
+// attention's 32-row stage) of every layer and KV head.
+q_error_code batch_init(DevState* s, uint32_t B, uint32_t page_rows = 0, uint32_t n_pages = 0) {
     if (!s->built || (s->tp_world > 1 && !s->comm)) return Q_ERR_INVALID_ARG;
     if (B == 0 || B > BT_MAXB) return Q_ERR_INVALID_SIZE;
     const q_llama_config& c = s->cfg;
@@ -218,11 +232,33 @@ q_error_code batch_init(DevState* s, uint32_t B) {
     b.tok_cap = c.max_seq_len;
     const size_t kv_seq = (size_t)c.n_layers * t.nkv * c.max_seq_len * 2 * s->hd * 4;
     b.kv_bytes_seq = kv_seq;
-    if (!cuda_ok(dev_malloc(&b.kv, kv_seq * B), "dev_malloc(batch kv)")) {
+    const uint32_t sp = ATT_STAGE_BYTES / (s->hd * 4);  // attention stage rows
+    if (page_rows) {
+        if (page_rows % sp || page_rows > c.max_seq_len || n_pages == 0) {
+            free_batch(s);
+            return Q_ERR_INVALID_SIZE;
+        }
+        b.page_rows = page_rows;
+        b.pages_per_seq = (c.max_seq_len + page_rows - 1) / page_rows;
+        b.n_pages = n_pages;
+    }
+    const size_t kv_alloc = page_rows ? (size_t)n_pages * c.n_layers * t.nkv * page_rows * 2 * s->hd * 4 : kv_seq * B;
+    if (!cuda_ok(dev_malloc(&b.kv, kv_alloc), "dev_malloc(batch kv)")) {
         free_batch(s);
         return Q_ERR_ALLOC_FAILED;
     }
-    Q_CUDA(cudaMemset(b.kv, 0, kv_seq * B));
+    Q_CUDA(cudaMemset(b.kv, 0, kv_alloc));
+    if (page_rows) {
+        const size_t np = (size_t)B * b.pages_per_seq;
+        if (!cuda_ok(dev_malloc(&b.d_pages, np * 4), "dev_malloc(page table)")) {
+            free_batch(s);
+            return Q_ERR_ALLOC_FAILED;
+        }
+        Q_CUDA(cudaMemset(b.d_pages, 0, np * 4));
+        b.h_pages.assign(np, kNoPage);
+        b.free_pages.resize(n_pages);
+        for (uint32_t i = 0; i < n_pages; ++i) b.free_pages[i] = n_pages - 1 - i;  // pops 0, 1, 2, ...
+    }
     if (s->tp_world > 1 &&
         !cuda_ok(dev_malloc(&b.gath, (size_t)s->tp_world * B * t.v_pad * 4), "dev_malloc(batch logits gather)")) {
         free_batch(s);
@@ -314,8 +350,12 @@ q_error_code batch_init(DevState* s, uint32_t B) {
             return Q_ERR_INVALID_ARG;
         }
         const uint32_t hd = s->hd;
-        const cuuint64_t dims[3] = {2ull * hd, c.max_seq_len, (cuuint64_t)B * c.n_layers * t.nkv};
-        const cuuint64_t strides[2] = {2ull * hd * 4, 2ull * hd * 4 * c.max_seq_len};
+        // contiguous: planes (b * L + layer) * n_kv + head of max_seq rows;
+        // paged: planes (page * L + layer) * n_kv + head of page_rows rows
+        const cuuint64_t rows = page_rows ? page_rows : c.max_seq_len;
+        const cuuint64_t planes = (cuuint64_t)(page_rows ? n_pages : B) * c.n_layers * t.nkv;
+        const cuuint64_t dims[3] = {2ull * hd, rows, planes};
+        const cuuint64_t strides[2] = {2ull * hd * 4, 2ull * hd * 4 * rows};
         const cuuint32_t box[3] = {hd, ATT_STAGE_BYTES / (4 * hd), 1};
         const cuuint32_t estr[3] = {1, 1, 1};
         if (encode(&b.kv_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, b.kv, dims, strides, box, estr,
@@ -348,11 +388,64 @@ q_error_code batch_init(DevState* s, uint32_t B) {
     return Q_OK;
 }
 
+// Paged caches: give sequence seq pages for its rows [0, rows) (zeroed when
+// first given, as a contiguous cache starts zeroed).  Q_ERR_ARENA_OOM when
+// the pool is exhausted.
+static q_error_code batch_cover(DevState* s, uint32_t seq, uint64_t rows) {
+    BatchState& b = s->batch;
+    const uint64_t n = std::min<uint64_t>((rows + b.page_rows - 1) / b.page_rows, b.pages_per_seq);
+    const size_t page_bytes = (size_t)s->cfg.n_layers * s->tp.nkv * b.page_rows * 2 * s->hd * 4;
+    for (uint64_t r = 0; r < n; ++r) {
+        uint32_t& e = b.h_pages[(size_t)seq * b.pages_per_seq + r];
+        if (e != kNoPage) continue;
+        if (b.free_pages.empty()) return Q_ERR_ARENA_OOM;
+        e = b.free_pages.back();
+        b.free_pages.pop_back();
+        Q_CUDA(cudaMemsetAsync((uint8_t*)b.kv + (size_t)e * page_bytes, 0, page_bytes, s->stream));
+        b.pages_dirty = true;
+    }
+    return Q_OK;
+}
+
+// The page table to the device before the next step reads it.
+static q_error_code batch_sync_pages(DevState* s) {
+    BatchState& b = s->batch;
+    if (!b.d_pages || !b.pages_dirty) return Q_OK;
+    Q_CUDA(cudaStreamSynchronize(s->stream));
+    Q_CUDA(cudaMemcpy(b.d_pages, b.h_pages.data(), b.h_pages.size() * 4, cudaMemcpyHostToDevice));
+    b.pages_dirty = false;
+    return Q_OK;
+}
+
 }  // namespace qb200
 
 using namespace qb200;
 
 extern "C" {
+
+q_error_code q_b200_batch_init_paged(q_context* ctx, q_llama_model* model, uint32_t batch, uint32_t page_rows,
+                                     uint32_t n_pages) {
+    if (!ctx || !model || page_rows == 0) return Q_ERR_INVALID_ARG;
+    DevState* s = state_of(ctx, false);
+    if (!s) return Q_ERR_INVALID_ARG;
+    return batch_init(s, batch, page_rows, n_pages);
+}
+
+q_error_code q_b200_batch_release(q_context* ctx, uint32_t seq) {
+    if (!ctx) return Q_ERR_INVALID_ARG;
+    DevState* s = state_of(ctx, false);
+    if (!s || !s->batch.kv || seq >= s->batch.B) return Q_ERR_INVALID_ARG;
+    BatchState& b = s->batch;
+    if (!b.d_pages) return Q_OK;  // contiguous caches: nothing to give back
+    for (uint32_t r = 0; r < b.pages_per_seq; ++r) {
+        uint32_t& e = b.h_pages[(size_t)seq * b.pages_per_seq + r];
+        if (e == kNoPage) continue;
+        b.free_pages.push_back(e);
+        e = kNoPage;
+        b.pages_dirty = true;
+    }
+    return Q_OK;
+}
 
 q_error_code q_b200_batch_init(q_context* ctx, q_llama_model* model, uint32_t batch) {
     if (!ctx || !model) return Q_ERR_INVALID_ARG;
@@ -368,9 +461,40 @@ static q_error_code batch_kv_io(q_context* ctx, uint32_t seq, size_t off, void* 
     if (seq >= s->batch.B) return Q_ERR_INVALID_ARG;
     const size_t n = s->batch.kv_bytes_seq;
     if (off > n || bytes > n - off) return Q_ERR_INVALID_SIZE;
-    uint8_t* d = (uint8_t*)s->batch.kv + (size_t)seq * n + off;
-    Q_CUDA(cudaStreamSynchronize(s->stream));
-    Q_CUDA(write ? cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) : cudaMemcpy(host, d, bytes, cudaMemcpyDeviceToHost));
+    BatchState& b = s->batch;
+    if (!b.d_pages) {
+        uint8_t* d = (uint8_t*)b.kv + (size_t)seq * n + off;
+        Q_CUDA(cudaStreamSynchronize(s->stream));
+        Q_CUDA(write ? cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice)
+                     : cudaMemcpy(host, d, bytes, cudaMemcpyDeviceToHost));
+        return Q_OK;
+    }
+    // paged: whole rows of the upstream layout [L][n_kv][max_seq][K|V], copied
+    // page by page; reading a row that has no page gives zeros
+    const q_llama_config& c = s->cfg;
+    const size_t rb = (size_t)2 * s->hd * 4, nkv = s->tp.nkv, ms = c.max_seq_len;
+    if (off % rb || bytes % rb) return Q_ERR_INVALID_SIZE;
+    const size_t page_bytes = (size_t)c.n_layers * nkv * b.page_rows * rb;
+    for (size_t i = off / rb, end = (off + bytes) / rb; i < end;) {
+        const size_t layer = i / (nkv * ms), head = (i / ms) % nkv, p = i % ms;
+        const size_t r = p / b.page_rows, in = p % b.page_rows;
+        const size_t run = std::min<size_t>({end - i, b.page_rows - in, ms - p});  // rows in this page and plane
+        uint8_t* h = (uint8_t*)host + (i * rb - off);
+        if (write) {
+            q_error_code rc = batch_cover(s, seq, (uint64_t)(r + 1) * b.page_rows);
+            if (rc != Q_OK) return rc;
+        }
+        const uint32_t pg = b.h_pages[(size_t)seq * b.pages_per_seq + r];
+        if (pg == kNoPage) {
+            std::memset(h, 0, run * rb);
+        } else {
+            uint8_t* d = (uint8_t*)b.kv + pg * page_bytes + ((layer * nkv + head) * b.page_rows + in) * rb;
+            Q_CUDA(cudaStreamSynchronize(s->stream));
+            Q_CUDA(write ? cudaMemcpy(d, h, run * rb, cudaMemcpyHostToDevice)
+                         : cudaMemcpy(h, d, run * rb, cudaMemcpyDeviceToHost));
+        }
+        i += run;
+    }
     return Q_OK;
 }
 
@@ -393,6 +517,14 @@ q_error_code q_b200_decode_batch_loop(q_llama_model* model, q_context* ctx, cons
     for (uint32_t i = 0; i < b.B; ++i) {
         if (tokens[i] >= c.vocab_size) return Q_ERR_INVALID_ARG;
         if ((uint64_t)pos[i] + n_steps > c.max_seq_len) return Q_ERR_INVALID_ARG;
+    }
+    if (b.d_pages) {  // pages for every row the steps read or write
+        for (uint32_t i = 0; i < b.B; ++i) {
+            const q_error_code rc = batch_cover(s, i, (uint64_t)pos[i] + n_steps);
+            if (rc != Q_OK) return rc;
+        }
+        const q_error_code rc = batch_sync_pages(s);
+        if (rc != Q_OK) return rc;
     }
     Q_CUDA(cudaStreamSynchronize(s->stream));  // h_step may still be read by a prior copy
     for (uint32_t i = 0; i < b.B; ++i) {

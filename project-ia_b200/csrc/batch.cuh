@@ -161,8 +161,11 @@ struct BatchGemvArgs {
     const float* rope_cos;
     const float* rope_sin;
     float* kv;               // cache of sequence 0, this layer's plane [n_kv][max_seq][2 hd]
+                             // (paged: the page pool, [page][n_layers][n_kv][page_rows][2 hd])
     size_t kv_seq_stride;    // floats from one sequence's cache to the next
     uint32_t hd, q_rows, kv_rows, max_seq;
+    const uint32_t* pages;   // paged caches: [B][pages_per_seq] page of each page_rows rows
+    uint32_t page_rows, pages_per_seq, n_layers, layer;
 };
 
 __device__ __forceinline__ uint32_t nib2h(uint32_t w, uint32_t sel) {
@@ -201,7 +204,13 @@ __device__ __forceinline__ void bt_epilogue(const BatchGemvArgs& a, uint32_t r0,
         const float* ct = a.rope_cos + (size_t)p * a.hd;
         const float* st = a.rope_sin + (size_t)p * a.hd;
         float o0, o1;
-        float* cache = a.kv + (size_t)b * a.kv_seq_stride;
+        // row p of head h in sequence b's cache
+        auto row = [&](uint32_t h) -> float* {
+            if (!a.pages) return a.kv + (size_t)b * a.kv_seq_stride + ((size_t)h * a.max_seq + p) * 2 * a.hd;
+            const uint32_t pg = __ldg(a.pages + (size_t)b * a.pages_per_seq + p / a.page_rows);
+            const uint32_t nkv = a.kv_rows / a.hd;
+            return a.kv + ((((size_t)pg * a.n_layers + a.layer) * nkv + h) * a.page_rows + p % a.page_rows) * 2 * a.hd;
+        };
         if (r0 < a.q_rows) {
             rope_pair(v0, v1, ct, st, r0 % a.hd, o0, o1);
             yr[r0] = o0;
@@ -209,12 +218,12 @@ __device__ __forceinline__ void bt_epilogue(const BatchGemvArgs& a, uint32_t r0,
         } else if (r0 < a.q_rows + a.kv_rows) {
             const uint32_t kr = r0 - a.q_rows, h = kr / a.hd, e = kr % a.hd;
             rope_pair(v0, v1, ct, st, e, o0, o1);
-            float* dst = cache + ((size_t)h * a.max_seq + p) * 2 * a.hd + e;
+            float* dst = row(h) + e;
             dst[0] = o0;
             dst[1] = o1;
         } else {
             const uint32_t vr = r0 - a.q_rows - a.kv_rows, h = vr / a.hd, e = vr % a.hd;
-            float* dst = cache + ((size_t)h * a.max_seq + p) * 2 * a.hd + a.hd + e;
+            float* dst = row(h) + a.hd + e;
             dst[0] = v0;
             dst[1] = v1;
         }

@@ -132,6 +132,14 @@ struct BatchState {
     // parallelism enough for fewer, longer chunks per sequence
     uint32_t att_cs = 0, att_ca = 0, att_slots = 0;
     size_t att_smem = 0;
+    // paged caches (q_b200_batch_init_paged): kv is a pool of n_pages pages,
+    // each [L][n_kv][page_rows][K|V]; d_pages[b * pages_per_seq + r] is the
+    // page holding sequence b's rows [r * page_rows, (r + 1) * page_rows)
+    uint32_t page_rows = 0, pages_per_seq = 0, n_pages = 0;
+    uint32_t* d_pages = nullptr;
+    std::vector<uint32_t> h_pages;     // host mirror, kNoPage where unassigned
+    std::vector<uint32_t> free_pages;  // stack of unassigned pages
+    bool pages_dirty = false;
     cudaGraphExec_t graph = nullptr;
     uint64_t kernels = 0;
 };

@@ -136,6 +136,8 @@ _SIGS = {
     "q_b200_profile_step": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp]),
     "q_b200_device_logits": (_vp, [_vp]),
     "q_b200_batch_init": (_i, [_vp, _vp, _u32]),
+    "q_b200_batch_init_paged": (_i, [_vp, _vp, _u32, _u32, _u32]),
+    "q_b200_batch_release": (_i, [_vp, _u32]),
     "q_b200_batch_kv_write": (_i, [_vp, _u32, _sz, _vp, _sz]),
     "q_b200_batch_kv_read": (_i, [_vp, _u32, _sz, _vp, _sz]),
     "q_b200_decode_batch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp]),

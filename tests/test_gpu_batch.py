@@ -117,3 +117,82 @@ def test_llama70b_shapes_batch16_vs_oracle(llama70b_2layer):
     path, cfg = llama70b_2layer
     lens = [300 + 41 * b for b in range(16)]
     run_batch_vs_oracle(path, cfg, 16, lens, steps=2, seed=21)
+
+
+def _paged_vs_contiguous(path, cfg, B, lens, page_rows, seed):
+    """The same batched steps on contiguous caches and on a page pool sized
+    for the rows actually used: logits, tokens and caches must be identical
+    (the same arithmetic, only the addresses differ)."""
+    dev = Q.Model(path)
+    V = cfg.vocab_size
+    n_elems = cfg.n_layers * cfg.n_kv_heads * cfg.max_seq_len * 2 * (cfg.dim // cfg.n_heads)
+    kvs = []
+    for b in range(B):
+        kv = np.zeros(n_elems, np.float32)
+        assert Q.lib.q_b200_fill_kv_prefill(Q.ptr(kv), C.byref(cfg), lens[b], seed + b, 0) == 0
+        kvs.append(kv)
+    toks = np.zeros(B, np.uint32)
+    Q.lib.q_b200_fill_tokens(Q.ptr(toks), B, seed, 3, 0, V)
+    pos = np.array(lens, np.uint32)
+    steps = 6
+
+    def run(paged):
+        if paged:
+            need = sum((ln + 1 + steps + page_rows - 1) // page_rows for ln in lens)
+            Q.check(Q.lib.q_b200_batch_init_paged(C.byref(dev.ctx), C.byref(dev.model), B, page_rows, need),
+                    "batch_init_paged")
+        else:
+            Q.check(Q.lib.q_b200_batch_init(C.byref(dev.ctx), C.byref(dev.model), B), "batch_init")
+        for b in range(B):
+            # only the rows the prefill wrote: the rest of a paged cache has no pages yet
+            rows = np.ascontiguousarray(kvs[b].reshape(cfg.n_layers * cfg.n_kv_heads, cfg.max_seq_len, -1)[:, : lens[b]])
+            hd2 = rows.shape[-1]
+            for plane in range(rows.shape[0]):
+                off = (plane * cfg.max_seq_len) * hd2 * 4
+                Q.check(Q.lib.q_b200_batch_kv_write(C.byref(dev.ctx), b, off, Q.ptr(rows[plane]), rows[plane].nbytes),
+                        "kv_write")
+        logits = np.zeros(B * V, np.float32)
+        nxt = np.zeros(B, np.uint32)
+        Q.check(Q.lib.q_b200_decode_batch(C.byref(dev.model), C.byref(dev.ctx), Q.ptr(toks), Q.ptr(pos),
+                                          Q.ptr(logits), Q.ptr(nxt)), "decode_batch")
+        out = np.zeros(steps * B, np.uint32)
+        p1 = (pos + 1).astype(np.uint32)
+        Q.check(Q.lib.q_b200_decode_batch_loop(C.byref(dev.model), C.byref(dev.ctx), Q.ptr(nxt), Q.ptr(p1), steps,
+                                               Q.ptr(out), 1), "decode_batch_loop")
+        caches = []
+        for b in range(B):
+            kv = np.zeros(n_elems, np.float32)
+            Q.check(Q.lib.q_b200_batch_kv_read(C.byref(dev.ctx), b, 0, Q.ptr(kv), kv.nbytes), "kv_read")
+            caches.append(kv)
+        return logits, out, caches
+
+    lc, oc, cc = run(False)
+    lp, op, cp = run(True)
+    np.testing.assert_array_equal(lp, lc)
+    np.testing.assert_array_equal(op, oc)
+    for b in range(B):
+        np.testing.assert_array_equal(cp[b], cc[b])
+    # a pool one page short of the next step fails cleanly, and releasing a
+    # sequence's pages lets the same step go through
+    Q.check(Q.lib.q_b200_batch_init_paged(C.byref(dev.ctx), C.byref(dev.model), B, page_rows,
+                                          sum((ln + 1 + page_rows - 1) // page_rows for ln in lens) - 1), "init")
+    nxt = np.zeros(B, np.uint32)
+    rc = Q.lib.q_b200_decode_batch(C.byref(dev.model), C.byref(dev.ctx), Q.ptr(toks), Q.ptr(pos), None, Q.ptr(nxt))
+    assert rc == -8  # Q_ERR_ARENA_OOM
+    big = int(np.argmax(lens))  # the longest sequence restarts from position 0 in an empty slot
+    Q.check(Q.lib.q_b200_batch_release(C.byref(dev.ctx), big), "release")
+    pos0 = pos.copy()
+    pos0[big] = 0
+    Q.check(Q.lib.q_b200_decode_batch(C.byref(dev.model), C.byref(dev.ctx), Q.ptr(toks), Q.ptr(pos0), None,
+                                      Q.ptr(nxt)), "decode_batch after release")
+    dev.close()
+
+
+def test_tiny_paged_matches_contiguous(tiny_path):
+    cfg = Q.config(**Q.TINY)
+    _paged_vs_contiguous(tiny_path, cfg, 5, [3, 130, 29, 255, 200], page_rows=128, seed=31)
+
+
+def test_llama70b_shapes_paged_matches_contiguous(llama70b_2layer):
+    path, cfg = llama70b_2layer
+    _paged_vs_contiguous(path, cfg, 16, [300 + 41 * b for b in range(16)], page_rows=64, seed=41)
